@@ -1,0 +1,409 @@
+#!/usr/bin/env python
+"""MoE-layer tokens/s on B200 (BASELINE metric) for EasyInfra's expert-parallel MoE
+layer forward, one process per GPU.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+A step is one forward pass of the whole MoE stack of the workload (every layer with
+its own weights and placement) over one batch of synthetic tokens per rank:
+router -> permute -> dispatch all-to-all -> grouped SwiGLU + down GEMMs -> combine
+all-to-all -> weighted unpermute (+ shared expert where the model has one).  Layers
+are chained (layer l+1 consumes layer l's output).  Each rank serves its own batch
+(attention is data-parallel in the reference), so per-GPU work is fixed as N grows
+("weak" scaling); value = tokens of all ranks x layers / max-over-ranks step time.
+
+Prints one JSON line on rank 0.  `--impl reference` times the reference's eager
+path (the CPU oracle restating it) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+METRIC = "MoE-layer tokens/s"
+UNIT = "tokens/s"
+
+# name -> (config key, phase, tokens per rank)
+WORKLOADS = {
+    "mixtral-prefill": ("mixtral", "prefill", 16384),
+    "mixtral-decode": ("mixtral", "decode", 64),
+    "qwen15-decode": ("qwen15", "decode", 128),
+    "dsv2lite-prefill": ("dsv2lite", "prefill", 16384),
+    "qwen3-decode-b1": ("qwen3", "decode", 1),
+    "qwen3-decode-b16": ("qwen3", "decode", 16),
+    "qwen3-decode-b64": ("qwen3", "decode", 64),
+    "qwen3-decode-b256": ("qwen3", "decode", 256),
+}
+DEFAULT_WORKLOAD = "mixtral-prefill"
+SECONDARY = {"mixtral-prefill": ["mixtral-decode"]}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (invalid as a result)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_sample(cfg_key: str, tokens: int, target_s: float = 3.0, layer: int = 0):
+    """Time the reference's eager MoE path (oracle restatement) on the host cores for
+    one layer on a bounded token sample; returns (tokens/s, sample description, cores)."""
+    from easyinfra_b200 import configs as C
+    from oracle import moe_oracle as O
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    shape = C.CONFIGS[cfg_key]
+    E = shape.num_experts
+    phy2log = torch.arange(E).view(1, E)
+    gw = C.router_weight(shape, layer)
+    gb = C.gate_bias(shape, layer)
+    wgu, wd = C.expert_weights(shape, layer, list(range(E)))
+    sgu, sd = C.shared_weights(shape, layer)
+    lw = O.LayerWeights(gw[:E], wgu, wd, None if gb is None else gb.to(shape.dtype), sgu, sd,
+                        gw[E] if shape.shared_gate else None)
+
+    def run(n):
+        x = C.hidden_states(shape, n)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            tr = O.moe_layer_ep([x], lw, shape.top_k, shape.norm_topk_prob, phy2log, use_eplb=False)[0]
+            O.layer_output(tr)
+        return time.perf_counter() - t0
+
+    n = min(tokens, 32)
+    run(n)
+    dt = run(n)
+    while dt < target_s / 4 and n < tokens:
+        n = min(tokens, n * 4)
+        dt = run(n)
+    sample = f"1 layer ({shape.name} layer {layer}), {n} of {tokens} tokens per sample, bf16 eager on CPU"
+    return n, dt, sample, cores, run
+
+
+def run_reference(args):
+    cfg_key, phase, tokens = WORKLOADS[args.workload]
+    n, _, sample, cores, run = cpu_sample(cfg_key, tokens)
+    for _ in range(args.warmup):
+        run(n)
+    times = [run(n) for _ in range(args.steps)]
+    ms = statistics.median(times) * 1e3
+    value = n / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "tokens_per_rank": tokens, "phase": phase},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            gid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", gid, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[0]))
+                mx = max(mx, float(r[1]))
+                for nm, v in zip(names, r[3:7]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- our arm
+def build_stack(cfg_key, rank, world, device, group, n_layers):
+    from easyinfra_b200 import configs as C
+    from easyinfra_b200.layer import LayerParams, MoELayer
+    from easyinfra_b200.placement import Placement
+
+    shape = C.CONFIGS[cfg_key]
+    E = shape.num_experts
+    layers = []
+    for l in range(n_layers):
+        if shape.placement and (world > 1 or E % world):
+            pl = Placement(C.load_placement(shape.placement, l, world), E)
+        else:
+            pl = Placement.default(E, world)
+        gw = C.router_weight(shape, l, device=device)
+        gb = C.gate_bias(shape, l)
+        wgu, wd = C.expert_weights(shape, l, pl.slots_of_rank(rank), device=device, fast=True)
+        sgu = sd = None
+        if shape.shared_intermediate:
+            g = torch.Generator(device=device)
+            g.manual_seed(C.layer_seed(shape, l, 3))
+            Is, H = shape.shared_intermediate, shape.hidden
+            sgu = torch.randn(2 * Is, H, generator=g, device=device, dtype=shape.dtype).mul_(0.02)
+            sd = torch.randn(H, Is, generator=g, device=device, dtype=shape.dtype).mul_(0.02)
+        params = LayerParams(gw, wgu, wd, None if gb is None else gb.to(shape.dtype).float().to(device),
+                             sgu, sd)
+        layers.append(MoELayer(params, pl, shape.top_k, shape.norm_topk_prob, rank=rank, group=group,
+                               shared_gate=shape.shared_gate))
+    return shape, layers
+
+
+def run_ours(args):
+    import torch.distributed as dist
+    from easyinfra_b200 import build, ops
+    from easyinfra_b200 import configs as C
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    build.build()
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+        group = dist.group.WORLD
+    cfg_key, phase, tokens = WORKLOADS[args.workload]
+    shape = C.CONFIGS[cfg_key]
+    n_layers = args.layers or shape.num_layers
+    shape, layers = build_stack(cfg_key, rank, world, device, group, n_layers)
+    hbm, bf16_burst, bf16_sus, peak_kind = peaks()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    results = {}
+
+    def measure(wl_name, with_roofline):
+        cfg_key_w, phase_w, T = WORKLOADS[wl_name]
+        x = C.hidden_states(shape, T, rank=rank, device=device)
+        bufs = [torch.empty_like(x), torch.empty_like(x)]
+
+        def step(inp):
+            h = inp
+            for i, lay in enumerate(layers):
+                h = lay.forward(h, out=bufs[i % 2])
+            return h
+
+        for _ in range(args.warmup):
+            step(x)
+        torch.cuda.synchronize()
+        # routing statistics of this input for the algorithmic roofline numbers
+        rows, hit = [], []
+        h = x
+        for i, lay in enumerate(layers):
+            st = lay.route_and_permute(h)
+            h = lay.forward(h, out=bufs[i % 2])
+            rows.append(st)
+        torch.cuda.synchronize()
+        layer_rows, layer_hit = [], []
+        for lay, st in zip(layers, rows):
+            c = st.route.slot_counts.view(lay.G, lay.P).cpu()
+            if lay.G == 1:
+                layer_rows.append(int(c.sum()))
+                layer_hit.append(int((c[0] > 0).sum()))
+            else:
+                layer_rows.append(None)
+                layer_hit.append(None)
+        del rows
+        # device-timed region
+        ev = []
+
+        def hook(name, ph):
+            if name == "grouped_swiglu":
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                ev.append(e)
+
+        sampler = ClockSampler(local_rank) if with_roofline else None
+        barrier()
+        torch.cuda.synchronize()
+        ops.LAUNCHES["count"] = 0
+        ops.EVENT_HOOK["fn"] = hook if with_roofline else None
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step(x)
+        t1.record()
+        torch.cuda.synchronize()
+        ops.EVENT_HOOK["fn"] = None
+        launches = ops.LAUNCHES["count"]
+        barrier()
+        clocks = sampler.stop() if sampler else None
+        ms = t0.elapsed_time(t1) / args.steps
+        ms = max_over_ranks(ms)
+        kernel_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev) - 1, 2)]
+        # e2e: host buffers, H2D of the input and D2H of the result inside the region
+        xh = x.cpu().pin_memory()
+        oh = torch.empty_like(xh).pin_memory()
+        xd = torch.empty_like(x)
+        for _ in range(args.warmup):
+            xd.copy_(xh, non_blocking=True)
+            oh.copy_(step(xd), non_blocking=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            xd.copy_(xh, non_blocking=True)
+            oh.copy_(step(xd), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        tok = T * world * len(layers)
+        res = {"workload": wl_name, "T": T, "ms": ms, "value": tok / (ms / 1e3),
+               "e2e_value": tok / (e2e_ms / 1e3), "e2e_ms": e2e_ms,
+               "h2d": xh.numel() * xh.element_size() * world, "d2h": oh.numel() * oh.element_size() * world,
+               "launches": launches // args.steps * args.steps, "clocks": clocks}
+        if with_roofline and kernel_ms and layer_rows[0] is not None:
+            # algorithmic work of the SwiGLU GEMM per launch, averaged over layers
+            H, I = shape.hidden, shape.intermediate
+            flops = [4.0 * r * I * H for r in layer_rows]
+            byts = [h * 2 * I * H * 2 + r * H * 2 + r * I * 2 for r, h in zip(layer_rows, layer_hit)]
+            per_launch_ms = statistics.mean(kernel_ms)
+            if phase_w == "prefill":
+                ach = statistics.mean(flops) / (per_launch_ms / 1e3) / 1e12
+                res["roofline"] = {"kernel": "grouped_swiglu", "bound": "tensor", "achieved": ach,
+                                   "peak": bf16_sus, "unit": "TFLOP/s", "frac": ach / bf16_sus,
+                                   "peak_kind": f"{peak_kind} bf16 sustained",
+                                   "kernel_ms": per_launch_ms, "traffic": traffic_for(wl_name)}
+            else:
+                ach = statistics.mean(byts) / (per_launch_ms / 1e3) / 1e9
+                res["roofline"] = {"kernel": "grouped_swiglu", "bound": "hbm", "achieved": ach,
+                                   "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                                   "peak_kind": f"{peak_kind} HBM copy",
+                                   "kernel_ms": per_launch_ms, "traffic": traffic_for(wl_name)}
+        return res
+
+    main = measure(args.workload, with_roofline=True)
+    secondary = []
+    if not args.no_secondary:
+        for wl in SECONDARY.get(args.workload, []):
+            if WORKLOADS[wl][0] == cfg_key:
+                s = measure(wl, with_roofline=True)
+                secondary.append({k: s[k] for k in ("workload", "value", "ms", "e2e_value") if k in s}
+                                 | ({"roofline": s["roofline"]} if "roofline" in s else {}))
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n, _, sample, cores, run = cpu_sample(cfg_key, tokens)
+        ts = [run(n) for _ in range(3)]
+        cpu = {"value": n / statistics.median(ts), "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": sample}
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": main["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": main["ms"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{shape.name} {args.workload} stack", "layers": len(layers),
+                   "tokens_per_rank": main["T"], "hidden": shape.hidden, "experts": shape.num_experts,
+                   "top_k": shape.top_k, "intermediate": shape.intermediate,
+                   "parallelism": f"ep{world}", "l2": "inputs larger than L2 (per-layer weights "
+                   f"{3 * shape.hidden * shape.intermediate * 2 * shape.num_experts / 1e9:.2f} GB)"},
+        "e2e": {"value": main["e2e_value"], "unit": UNIT, "h2d_bytes_per_step": main["h2d"],
+                "d2h_bytes_per_step": main["d2h"], "ms_per_step": main["e2e_ms"]},
+        "gpu_launches": main["launches"],
+        "roofline": main.get("roofline"),
+        "cpu_baseline": cpu,
+        "clocks": main["clocks"],
+        "secondary": secondary,
+    }
+    if args.layers:
+        line["config"]["debug_reduced_layers"] = True
+    print(json.dumps(line), flush=True)
+
+
+def traffic_for(workload: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
+    (profiles/traffic.json), or None when no capture exists for this workload."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f).get(workload)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        run_reference(args)
+        return
+    run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

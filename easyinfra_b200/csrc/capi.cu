@@ -1,0 +1,411 @@
+// C-ABI entry points of libb200moe.so (declared in include/b200moe.h).
+//
+// This layer validates arguments, lays out the router workspace, picks kernel
+// configurations and launches on the caller's stream.  It never allocates device
+// memory and never throws across the ABI.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/b200moe.h"
+#include "kernels.cuh"
+
+namespace b200moe {
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// ------------------------------------------------------------------ segment gather
+__global__ void __launch_bounds__(256) gather_segments_kernel(const uint8_t* src, uint8_t* dst,
+                                                              int64_t row_bytes,
+                                                              const int32_t* src_start,
+                                                              const int32_t* dst_start,
+                                                              const int32_t* len, int rows_per_cta,
+                                                              int32_t* dst_to_src) {
+  const int seg = blockIdx.y;
+  const int n = len[seg];
+  const int r0 = blockIdx.x * rows_per_cta;
+  if (r0 >= n) return;
+  const int r1 = min(n, r0 + rows_per_cta);
+  const int64_t vec = row_bytes / 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = r0 + warp; r < r1; r += blockDim.x >> 5) {
+    const uint4* s = reinterpret_cast<const uint4*>(src + (static_cast<int64_t>(src_start[seg]) + r) * row_bytes);
+    uint4* d = reinterpret_cast<uint4*>(dst + (static_cast<int64_t>(dst_start[seg]) + r) * row_bytes);
+    for (int64_t v = lane; v < vec; v += 32) d[v] = __ldg(s + v);
+    if (dst_to_src != nullptr && lane == 0) dst_to_src[dst_start[seg] + r] = src_start[seg] + r;
+  }
+}
+
+}  // namespace b200moe
+
+using namespace b200moe;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(B200MOE_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return B200MOE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr size_t kTicketBytes = 256;
+
+int tokens_per_block(int T) {
+  if (T >= 16384) return 32;
+  if (T >= 4096) return 16;
+  return 8;
+}
+
+int nblocks_for(int T) {
+  const int tb = tokens_per_block(T);
+  return (T + tb - 1) / tb;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+struct RouterWs {
+  uint32_t* ticket;
+  int32_t* block_counts;
+  float* logits;
+  size_t bytes;
+};
+
+RouterWs router_ws_layout(void* base, int T, int E1, int num_slots) {
+  RouterWs w;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  w.ticket = reinterpret_cast<uint32_t*>(p);
+  off += kTicketBytes;
+  w.block_counts = reinterpret_cast<int32_t*>(p + off);
+  off += align256(static_cast<size_t>(num_slots) * nblocks_for(T) * sizeof(int32_t));
+  w.logits = reinterpret_cast<float*>(p + off);
+  off += align256(static_cast<size_t>(T) * E1 * sizeof(float));
+  w.bytes = off;
+  return w;
+}
+
+int device_ok() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(B200MOE_ENODEVICE, "no CUDA device");
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return fail(B200MOE_ENODEVICE, "device %d is sm_%d0, this library is built for sm_100a", dev, major);
+  return B200MOE_OK;
+}
+
+int select_common(const float* logits, int has_shared_gate, int T, int E, int K, int renorm,
+                  float scale, int round_bf16, const int32_t* log2phy, const int32_t* rep_count,
+                  int max_rep, int num_slots, int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                  float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets,
+                  const RouterWs& ws, int* status, cudaStream_t stream) {
+  RouterSelectParams s;
+  s.logits = logits;
+  s.T = T;
+  s.E = E;
+  s.E1 = E + (has_shared_gate ? 1 : 0);
+  s.K = K;
+  s.renorm = renorm;
+  s.scale = scale;
+  s.round_bf16 = round_bf16;
+  s.has_shared_gate = has_shared_gate;
+  s.log2phy = log2phy;
+  s.rep_count = rep_count;
+  s.max_rep = max_rep;
+  s.num_slots = num_slots;
+  s.tb = tokens_per_block(T);
+  s.nblocks = nblocks_for(T);
+  s.topk_ids = topk_ids;
+  s.topk_w = topk_w;
+  s.phys_ids = phys_ids;
+  s.shared_gate = shared_gate;
+  s.block_counts = ws.block_counts;
+  s.slot_counts = slot_counts;
+  s.slot_offsets = slot_offsets;
+  s.ticket = ws.ticket;
+  s.status = status;
+  launch_router_select(s, stream);
+  return check_launch("router_select");
+}
+
+int check_select_args(int T, int E, int K, int num_slots, const int32_t* log2phy,
+                      const int32_t* rep_count, int max_rep, const void* topk_ids,
+                      const void* topk_w, const void* phys_ids, const void* slot_counts,
+                      const void* slot_offsets, int has_shared_gate, const void* shared_gate) {
+  if (T < 0) return fail(B200MOE_EINVAL, "T=%d < 0", T);
+  if (E < 1 || E > 256) return fail(B200MOE_EUNSUPPORTED, "E=%d outside [1, 256]", E);
+  if (K < 1 || K > 8 || K > E) return fail(B200MOE_EUNSUPPORTED, "K=%d outside [1, min(8, E)]", K);
+  if (num_slots < 1 || num_slots > 8192) return fail(B200MOE_EUNSUPPORTED, "num_slots=%d", num_slots);
+  if ((log2phy == nullptr) != (rep_count == nullptr))
+    return fail(B200MOE_EINVAL, "log2phy and rep_count must both be given or both be NULL");
+  if (log2phy == nullptr && num_slots < E)
+    return fail(B200MOE_EINVAL, "num_slots=%d < E=%d without a placement map", num_slots, E);
+  if (log2phy != nullptr && max_rep < 1) return fail(B200MOE_EINVAL, "max_rep=%d", max_rep);
+  if (!topk_ids || !topk_w || !phys_ids || !slot_counts || !slot_offsets)
+    return fail(B200MOE_EINVAL, "null output pointer");
+  if (has_shared_gate && !shared_gate) return fail(B200MOE_EINVAL, "shared_gate output is NULL");
+  return B200MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200moe_abi_version(void) { return B200MOE_ABI_VERSION; }
+
+const char* b200moe_last_error(void) { return g_err; }
+
+int b200moe_tokens_per_block(int T) { return tokens_per_block(T); }
+
+size_t b200moe_router_workspace_bytes(int T, int E1, int num_slots) {
+  if (T < 0 || E1 < 0 || num_slots < 0) return 0;
+  return router_ws_layout(nullptr, T, E1, num_slots).bytes;
+}
+
+int b200moe_router(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
+                   const float* gate_bias, int has_shared_gate, int T, int H, int E, int K,
+                   int renorm, float scale, const int32_t* log2phy, const int32_t* rep_count,
+                   int max_rep, int num_slots, int32_t* topk_ids, float* topk_w,
+                   int32_t* phys_ids, float* shared_gate, int32_t* slot_counts,
+                   int32_t* slot_offsets, float* logits_out, void* workspace,
+                   size_t workspace_bytes, int* status, void* stream) {
+  int rc = check_select_args(T, E, K, num_slots, log2phy, rep_count, max_rep, topk_ids, topk_w,
+                             phys_ids, slot_counts, slot_offsets, has_shared_gate, shared_gate);
+  if (rc) return rc;
+  if ((rc = device_ok())) return rc;
+  if (x_dtype != B200MOE_DTYPE_BF16 && x_dtype != B200MOE_DTYPE_F32)
+    return fail(B200MOE_EUNSUPPORTED, "x_dtype=%d", x_dtype);
+  if (!x || !gate_w || !workspace) return fail(B200MOE_EINVAL, "null input or workspace");
+  if (H <= 0 || H % 8 != 0) return fail(B200MOE_EUNSUPPORTED, "H=%d must be a positive multiple of 8", H);
+  if (ldx < H || (ldx * dtype_bytes(x_dtype)) % 16 != 0 || !aligned16(x) || !aligned16(gate_w))
+    return fail(B200MOE_EINVAL, "x/gate_w must be 16-byte aligned with 16-byte row stride (ldx=%lld)",
+                static_cast<long long>(ldx));
+  const int E1 = E + (has_shared_gate ? 1 : 0);
+  const RouterWs ws = router_ws_layout(workspace, T, E1, num_slots);
+  if (workspace_bytes < ws.bytes)
+    return fail(B200MOE_EINVAL, "workspace too small: %zu < %zu", workspace_bytes, ws.bytes);
+  if (T == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RouterLogitsParams lp;
+  lp.x = x;
+  lp.ldx = ldx;
+  lp.w = gate_w;
+  lp.bias = gate_bias;
+  lp.T = T;
+  lp.H = H;
+  lp.E1 = E1;
+  lp.logits = logits_out ? logits_out : ws.logits;
+  launch_router_logits(lp, x_dtype, st);
+  if ((rc = check_launch("router_logits"))) return rc;
+  return select_common(lp.logits, has_shared_gate, T, E, K, renorm, scale,
+                       x_dtype == B200MOE_DTYPE_BF16, log2phy, rep_count, max_rep, num_slots,
+                       topk_ids, topk_w, phys_ids, shared_gate, slot_counts, slot_offsets, ws,
+                       status, st);
+}
+
+int b200moe_router_from_logits(const float* logits, int has_shared_gate, int T, int E, int K,
+                               int renorm, float scale, int round_bf16, const int32_t* log2phy,
+                               const int32_t* rep_count, int max_rep, int num_slots,
+                               int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                               float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets,
+                               void* workspace, size_t workspace_bytes, int* status,
+                               void* stream) {
+  int rc = check_select_args(T, E, K, num_slots, log2phy, rep_count, max_rep, topk_ids, topk_w,
+                             phys_ids, slot_counts, slot_offsets, has_shared_gate, shared_gate);
+  if (rc) return rc;
+  if ((rc = device_ok())) return rc;
+  if (!logits || !workspace) return fail(B200MOE_EINVAL, "null logits or workspace");
+  const int E1 = E + (has_shared_gate ? 1 : 0);
+  const RouterWs ws = router_ws_layout(workspace, T, E1, num_slots);
+  if (workspace_bytes < ws.bytes)
+    return fail(B200MOE_EINVAL, "workspace too small: %zu < %zu", workspace_bytes, ws.bytes);
+  if (T == 0) return B200MOE_OK;
+  return select_common(logits, has_shared_gate, T, E, K, renorm, scale, round_bf16, log2phy,
+                       rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate,
+                       slot_counts, slot_offsets, ws, status, static_cast<cudaStream_t>(stream));
+}
+
+int b200moe_permute(const void* x, int64_t ldx, int x_dtype, int T, int H, int K, int E1,
+                    const int32_t* phys_ids, int num_slots, void* send, int32_t* pos_of,
+                    int64_t* send_token, int64_t* send_slot, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (x_dtype != B200MOE_DTYPE_BF16 && x_dtype != B200MOE_DTYPE_F32)
+    return fail(B200MOE_EUNSUPPORTED, "x_dtype=%d", x_dtype);
+  if (T < 0 || K < 1 || K > 8 || H <= 0) return fail(B200MOE_EINVAL, "T=%d K=%d H=%d", T, K, H);
+  const int row_bytes = H * dtype_bytes(x_dtype);
+  if (row_bytes % 16 != 0) return fail(B200MOE_EUNSUPPORTED, "row bytes %d not a multiple of 16", row_bytes);
+  if (!x || !phys_ids || !send || !pos_of || !workspace) return fail(B200MOE_EINVAL, "null pointer");
+  if (!aligned16(x) || !aligned16(send) || (ldx * dtype_bytes(x_dtype)) % 16 != 0)
+    return fail(B200MOE_EINVAL, "x/send must be 16-byte aligned with 16-byte row stride");
+  if (tokens_per_block(T) * K > 512) return fail(B200MOE_EUNSUPPORTED, "tokens per block * K > 512");
+  const RouterWs ws = router_ws_layout(workspace, T, E1, num_slots);
+  if (workspace_bytes < ws.bytes)
+    return fail(B200MOE_EINVAL, "workspace too small: %zu < %zu", workspace_bytes, ws.bytes);
+  if (T == 0) return B200MOE_OK;
+  PermuteParams p;
+  p.x = x;
+  p.x_stride = ldx * dtype_bytes(x_dtype);
+  p.row_bytes = row_bytes;
+  p.T = T;
+  p.K = K;
+  p.phys_ids = phys_ids;
+  p.block_offsets = ws.block_counts;
+  p.num_slots = num_slots;
+  p.nblocks = nblocks_for(T);
+  p.tb = tokens_per_block(T);
+  p.send = send;
+  p.pos_of = pos_of;
+  p.send_token = send_token;
+  p.send_slot = send_slot;
+  launch_permute(p, static_cast<cudaStream_t>(stream));
+  return check_launch("permute");
+}
+
+int b200moe_grouped_swiglu(const void* x, int64_t ldx, int64_t rows_cap,
+                           const int32_t* expert_offsets, int P, int H, int I,
+                           const void* w_gate_up, void* act, int64_t ld_act, int* status,
+                           void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (!x || !expert_offsets || !w_gate_up || !act) return fail(B200MOE_EINVAL, "null pointer");
+  if (P < 1 || H <= 0 || I <= 0 || rows_cap < 0) return fail(B200MOE_EINVAL, "P=%d H=%d I=%d", P, H, I);
+  if (H % 64 != 0 || I % 32 != 0)
+    return fail(B200MOE_EUNSUPPORTED, "grouped_swiglu needs H %% 64 == 0 and I %% 32 == 0 (H=%d I=%d)", H, I);
+  if (ldx < H || ldx % 8 != 0 || ld_act < I || ld_act % 8 != 0 || !aligned16(x) || !aligned16(act) ||
+      !aligned16(w_gate_up))
+    return fail(B200MOE_EINVAL, "bad leading dimension or alignment");
+  if (rows_cap == 0) return B200MOE_OK;
+  GemmLaunch L;
+  L.a = x;
+  L.rows_cap = rows_cap;
+  L.lda = ldx;
+  L.w = w_gate_up;
+  L.p.expert_offsets = expert_offsets;
+  L.p.P = P;
+  L.p.N = I;
+  L.p.K = H;
+  L.p.w_rows = 2 * I;
+  L.p.up_row = I;
+  L.p.out = act;
+  L.p.ldo = ld_act;
+  L.p.out_row_map = nullptr;
+  L.p.status = status;
+  rc = launch_grouped_swiglu(L, static_cast<cudaStream_t>(stream));
+  if (rc == -4) return fail(B200MOE_EUNSUPPORTED, "P=%d exceeds the kernel's slot limit", P);
+  if (rc == -1) return fail(B200MOE_ECUDA, "cuTensorMapEncodeTiled failed (gate_up)");
+  if (rc) return fail(B200MOE_ECUDA, "grouped_swiglu launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("grouped_swiglu");
+}
+
+int b200moe_grouped_down(const void* act, int64_t ld_act, int64_t rows_cap,
+                         const int32_t* expert_offsets, int P, int H, int I,
+                         const void* w_down, void* out, int64_t ldo,
+                         const int32_t* out_row_map, int* status, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (!act || !expert_offsets || !w_down || !out) return fail(B200MOE_EINVAL, "null pointer");
+  if (P < 1 || H <= 0 || I <= 0 || rows_cap < 0) return fail(B200MOE_EINVAL, "P=%d H=%d I=%d", P, H, I);
+  if (H % 32 != 0 || I % 64 != 0)
+    return fail(B200MOE_EUNSUPPORTED, "grouped_down needs H %% 32 == 0 and I %% 64 == 0 (H=%d I=%d)", H, I);
+  if (ld_act < I || ld_act % 8 != 0 || ldo < H || ldo % 8 != 0 || !aligned16(act) || !aligned16(out) ||
+      !aligned16(w_down))
+    return fail(B200MOE_EINVAL, "bad leading dimension or alignment");
+  if (rows_cap == 0) return B200MOE_OK;
+  GemmLaunch L;
+  L.a = act;
+  L.rows_cap = rows_cap;
+  L.lda = ld_act;
+  L.w = w_down;
+  L.p.expert_offsets = expert_offsets;
+  L.p.P = P;
+  L.p.N = H;
+  L.p.K = I;
+  L.p.w_rows = H;
+  L.p.up_row = 0;
+  L.p.out = out;
+  L.p.ldo = ldo;
+  L.p.out_row_map = out_row_map;
+  L.p.status = status;
+  rc = launch_grouped_down(L, static_cast<cudaStream_t>(stream));
+  if (rc == -4) return fail(B200MOE_EUNSUPPORTED, "P=%d exceeds the kernel's slot limit", P);
+  if (rc == -1) return fail(B200MOE_ECUDA, "cuTensorMapEncodeTiled failed (down)");
+  if (rc) return fail(B200MOE_ECUDA, "grouped_down launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("grouped_down");
+}
+
+int b200moe_combine(const void* y, int64_t ldy, int dtype, const int32_t* pos_of,
+                    const float* topk_w, int T, int K, int H, const void* shared, int64_t lds,
+                    const float* shared_gate, void* out, int64_t ldo, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (dtype != B200MOE_DTYPE_BF16 && dtype != B200MOE_DTYPE_F32)
+    return fail(B200MOE_EUNSUPPORTED, "dtype=%d", dtype);
+  if (T < 0 || K < 1 || K > 8 || H <= 0 || H % 8 != 0) return fail(B200MOE_EINVAL, "T=%d K=%d H=%d", T, K, H);
+  if (T == 0) return B200MOE_OK;
+  if (!y || !pos_of || !topk_w || !out) return fail(B200MOE_EINVAL, "null pointer");
+  const int eb = dtype_bytes(dtype);
+  if (!aligned16(y) || !aligned16(out) || (ldy * eb) % 16 || (ldo * eb) % 16 ||
+      (shared && (!aligned16(shared) || (lds * eb) % 16)))
+    return fail(B200MOE_EINVAL, "y/out/shared must be 16-byte aligned with 16-byte row strides");
+  CombineParams p;
+  p.y = y;
+  p.ldy = ldy;
+  p.dtype = dtype;
+  p.pos_of = pos_of;
+  p.topk_w = topk_w;
+  p.T = T;
+  p.K = K;
+  p.H = H;
+  p.shared = shared;
+  p.lds = lds;
+  p.shared_gate = shared_gate;
+  p.out = out;
+  p.ldo = ldo;
+  launch_combine(p, static_cast<cudaStream_t>(stream));
+  return check_launch("combine");
+}
+
+int b200moe_gather_segments(const void* src, void* dst, int64_t row_bytes,
+                            const int32_t* src_start, const int32_t* dst_start,
+                            const int32_t* len, int nseg, int64_t max_rows,
+                            int32_t* dst_to_src, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (nseg < 0 || nseg > 65535 || max_rows < 0) return fail(B200MOE_EINVAL, "nseg=%d max_rows=%lld", nseg, static_cast<long long>(max_rows));
+  if (nseg == 0 || max_rows == 0) return B200MOE_OK;
+  if (!src || !dst || !src_start || !dst_start || !len) return fail(B200MOE_EINVAL, "null pointer");
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || !aligned16(src) || !aligned16(dst))
+    return fail(B200MOE_EINVAL, "row_bytes=%lld must be a positive multiple of 16 with aligned buffers",
+                static_cast<long long>(row_bytes));
+  const int rows_per_cta = 16;
+  dim3 grid(static_cast<unsigned>((max_rows + rows_per_cta - 1) / rows_per_cta), static_cast<unsigned>(nseg));
+  gather_segments_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), row_bytes, src_start, dst_start, len,
+      rows_per_cta, dst_to_src);
+  return check_launch("gather_segments");
+}
+
+}  // extern "C"

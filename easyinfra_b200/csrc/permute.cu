@@ -1,0 +1,170 @@
+// Kernel family (2) and (4): token permutation and the weighted unpermute.
+//
+// permute_rows mirrors the reference's dispatch-side permutation
+//   idx          = phys_ids.view(-1).sort(stable=True).indices
+//   send_indices = idx // K ; send_topk = idx % K
+//   send         = x[send_indices]
+// (MoeAll2AllBlock.all2all_chunk_routing_compute, easyinfra/generation/blocks/moe/
+//  moe_all2all.py:345-351), without a sort: the router's last CTA already turned the
+// per-block slot histograms into absolute write offsets, so each CTA ranks its own
+// entries stably (flat index order within a slot) with warp match/ballot and writes
+// every token row to its K destinations with 16-byte vector stores.  Rows of one
+// destination rank are contiguous ([dst rank][local slot][token order]) because
+// physical slot ids are rank-major.
+//
+// combine_rows mirrors the reference's unpermute
+//   out = zeros(T, H); out.index_add_(0, send_indices, y * w[send_indices, send_topk])
+// (moe_all2all.py:291-307) as a gather: one warp per token reads its K expert rows,
+// accumulates w_k * y_k in fp32 and writes the token row once (no atomics).  The
+// optional shared-expert term adds gate[t] * shared[t] (gate == 1 when absent).
+#include "kernels.cuh"
+
+namespace b200moe {
+
+constexpr int PM_MAX_ENTRIES = 64 * 8;  // tb * K must not exceed this
+
+__global__ void __launch_bounds__(256) permute_rows(PermuteParams p) {
+  extern __shared__ int32_t running[];     // [num_slots], -1 == not yet touched
+  __shared__ int32_t pos[PM_MAX_ENTRIES];  // destination row of each entry of this block
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * p.tb;
+  const int nt = min(p.tb, p.T - t0);
+  const int ne = nt * p.K;
+  const int64_t flat0 = static_cast<int64_t>(t0) * p.K;
+
+  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) running[s] = -1;
+  __syncthreads();
+  if (warp == 0) {
+    // Stable rank within the block: entries in flat (t*K + k) order, 32 at a time.
+    for (int base = 0; base < ne; base += 32) {
+      const int i = base + lane;
+      const bool valid = i < ne;
+      const int s = valid ? p.phys_ids[flat0 + i] : -1 - lane;
+      const uint32_t peers = __match_any_sync(0xffffffffu, s);
+      const int leader = __ffs(peers) - 1;
+      int start = 0;
+      if (valid && lane == leader) {
+        int cur = running[s];
+        if (cur < 0) cur = p.block_offsets[static_cast<int64_t>(s) * p.nblocks + blockIdx.x];
+        start = cur;
+        running[s] = cur + __popc(peers);
+      }
+      start = __shfl_sync(0xffffffffu, start, leader);
+      if (valid) pos[i] = start + __popc(peers & ((1u << lane) - 1u));
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+
+  for (int i = threadIdx.x; i < ne; i += blockDim.x) {
+    const int d = pos[i];
+    p.pos_of[flat0 + i] = d;
+    if (p.send_token) p.send_token[d] = t0 + i / p.K;
+    if (p.send_slot) p.send_slot[d] = i % p.K;
+  }
+
+  // Row copies: one warp per token; the token row is read once and written K times.
+  const int vec_per_row = p.row_bytes / 16;
+  for (int lt = warp; lt < nt; lt += blockDim.x >> 5) {
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) +
+                                                      static_cast<int64_t>(t0 + lt) * p.x_stride);
+    for (int v = lane; v < vec_per_row; v += 32) {
+      const uint4 val = __ldg(src + v);
+      for (int k = 0; k < p.K; ++k) {
+        const int d = pos[lt * p.K + k];
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.send) +
+                                              static_cast<int64_t>(d) * p.row_bytes);
+        dst[v] = val;
+      }
+    }
+  }
+}
+
+template <typename E>
+__device__ __forceinline__ void load8(const E* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <typename E>
+__device__ __forceinline__ void store8(E* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+template <typename E>
+__global__ void __launch_bounds__(256) combine_rows(CombineParams p) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= p.T) return;
+  const int t = warp;
+  const E* y = static_cast<const E*>(p.y);
+  int rows[8];
+  float wts[8];
+  for (int k = 0; k < p.K; ++k) {
+    rows[k] = p.pos_of[static_cast<int64_t>(t) * p.K + k];
+    wts[k] = p.topk_w[static_cast<int64_t>(t) * p.K + k];
+  }
+  const float g = p.shared_gate ? p.shared_gate[t] : 1.f;
+  const E* sh = p.shared ? static_cast<const E*>(p.shared) + static_cast<int64_t>(t) * p.lds : nullptr;
+  E* out = static_cast<E*>(p.out) + static_cast<int64_t>(t) * p.ldo;
+  for (int c = lane * 8; c < p.H; c += 32 * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 0; k < p.K; ++k) {
+      float v[8];
+      load8<E>(y + static_cast<int64_t>(rows[k]) * p.ldy + c, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(wts[k], v[i], acc[i]);
+    }
+    if (sh) {
+      float v[8];
+      load8<E>(sh + c, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(g, v[i], acc[i]);
+    }
+    store8<E>(out + c, acc);
+  }
+}
+
+int launch_permute(const PermuteParams& p, cudaStream_t stream) {
+  if (p.T == 0) return 0;
+  const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t);
+  permute_rows<<<p.nblocks, 256, smem, stream>>>(p);
+  return 0;
+}
+
+int launch_combine(const CombineParams& p, cudaStream_t stream) {
+  if (p.T == 0) return 0;
+  const int grid = (p.T * 32 + 255) / 256;
+  if (p.dtype == kDtypeBF16)
+    combine_rows<__nv_bfloat16><<<grid, 256, 0, stream>>>(p);
+  else
+    combine_rows<float><<<grid, 256, 0, stream>>>(p);
+  return 0;
+}
+
+}  // namespace b200moe

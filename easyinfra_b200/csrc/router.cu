@@ -1,0 +1,344 @@
+// Kernel family (1): the MoE router.
+//
+// Mirrors the reference's routing for one chunk of tokens:
+//   logits = F.linear(x, W_gate, b_gate)            (Qwen3MoeSparseMoeBlock._routing,
+//   p      = softmax(logits, dtype=float32)          easyinfra/models/qwen3_moe/
+//   w, e   = topk(p, K)                               modeling_qwen3_moe.py:255-266)
+//   if norm_topk_prob: w = w / w.sum(-1)
+//   w      = w.to(x.dtype)
+// followed by the EPLB replica pick
+//   phys = log2phy[e][(t*K + k) % replica_count[e]]  (blocks/moe/base.py:40-64)
+// and the per-slot token histogram (blocks/moe/base.py:343-364).
+//
+// Three launches:
+//   router_logits_bf16  one warp per 16 tokens, mma.sync m16n8k16 bf16 -> fp32,
+//                       logits rounded to bf16 exactly like F.linear's bf16 output.
+//   router_logits_f32   SIMT fp32 dot products (fp32 activations).
+//   router_select       one warp per token: fp32 softmax, top-k with ties broken to
+//                       the lowest expert index, renorm, scaling, dtype rounding,
+//                       replica pick, per-block slot histogram; the last CTA to
+//                       finish turns the histograms into slot counts, slot offsets
+//                       and per-(slot, block) write offsets for the permute kernel.
+#include "kernels.cuh"
+
+namespace b200moe {
+
+// ------------------------------------------------------------------ logits (bf16)
+// CTA = 4 warps, 64 tokens.  x and W_gate chunks of 64 hidden elements are staged in
+// shared memory with a padded row stride; each warp owns 16 tokens and every
+// 8-expert column tile.
+constexpr int RL_TOK = 64;
+constexpr int RL_HC = 64;        // hidden elements per chunk
+constexpr int RL_LD = RL_HC + 8; // padded smem row (bf16 elements)
+constexpr int RL_MAXNT = 17;     // up to 136 logit columns per pass
+
+__global__ void __launch_bounds__(128) router_logits_bf16(RouterLogitsParams p, int cols_per_cta) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int col0 = blockIdx.y * cols_per_cta;
+  const int ncols = min(cols_per_cta, p.E1 - col0);
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);     // [64][RL_LD]
+  __nv_bfloat16* ws = xs + RL_TOK * RL_LD;                             // [ncols_pad][RL_LD]
+  const int nt = (ncols + 7) / 8;
+  const int ncols_pad = nt * 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok0 = blockIdx.x * RL_TOK;
+  const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
+  const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(p.w);
+
+  float acc[RL_MAXNT][4];
+#pragma unroll
+  for (int i = 0; i < RL_MAXNT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+  for (int h0 = 0; h0 < p.H; h0 += RL_HC) {
+    __syncthreads();
+    // stage x chunk: 64 rows x 64 bf16 = 8 x 16B per row
+    for (int i = threadIdx.x; i < RL_TOK * 8; i += 128) {
+      const int r = i >> 3, c = (i & 7) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      const int t = tok0 + r;
+      if (t < p.T && h0 + c < p.H) v = *reinterpret_cast<const uint4*>(x + t * p.ldx + h0 + c);
+      *reinterpret_cast<uint4*>(xs + r * RL_LD + c) = v;
+    }
+    for (int i = threadIdx.x; i < ncols_pad * 8; i += 128) {
+      const int r = i >> 3, c = (i & 7) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      const int e = col0 + r;
+      if (r < ncols && h0 + c < p.H) v = *reinterpret_cast<const uint4*>(w + static_cast<int64_t>(e) * p.H + h0 + c);
+      *reinterpret_cast<uint4*>(ws + r * RL_LD + c) = v;
+    }
+    __syncthreads();
+    const int ar = warp * 16 + (lane >> 2);
+    const int ac = (lane & 3) * 2;
+#pragma unroll
+    for (int k0 = 0; k0 < RL_HC; k0 += 16) {
+      uint32_t a0 = *reinterpret_cast<const uint32_t*>(xs + ar * RL_LD + k0 + ac);
+      uint32_t a1 = *reinterpret_cast<const uint32_t*>(xs + (ar + 8) * RL_LD + k0 + ac);
+      uint32_t a2 = *reinterpret_cast<const uint32_t*>(xs + ar * RL_LD + k0 + ac + 8);
+      uint32_t a3 = *reinterpret_cast<const uint32_t*>(xs + (ar + 8) * RL_LD + k0 + ac + 8);
+#pragma unroll
+      for (int j = 0; j < RL_MAXNT; ++j) {
+        if (j < nt) {
+          const int bn = j * 8 + (lane >> 2);
+          uint32_t b0 = *reinterpret_cast<const uint32_t*>(ws + bn * RL_LD + k0 + ac);
+          uint32_t b1 = *reinterpret_cast<const uint32_t*>(ws + bn * RL_LD + k0 + ac + 8);
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+              "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+              : "+f"(acc[j][0]), "+f"(acc[j][1]), "+f"(acc[j][2]), "+f"(acc[j][3])
+              : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        }
+      }
+    }
+  }
+  // C fragment: c0,c1 -> (row lane/4, cols 2*(lane%4)+{0,1}); c2,c3 -> row + 8.
+  const int r0 = tok0 + warp * 16 + (lane >> 2);
+#pragma unroll
+  for (int j = 0; j < RL_MAXNT; ++j) {
+    if (j < nt) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int row = r0 + (q >> 1) * 8;
+        const int col = j * 8 + (lane & 3) * 2 + (q & 1);
+        if (row < p.T && col < ncols) {
+          float v = acc[j][q];
+          if (p.bias) v += p.bias[col0 + col];
+          p.logits[static_cast<int64_t>(row) * p.E1 + col0 + col] = bf16_round(v);
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ logits (fp32)
+// One warp per token; lanes stride over the hidden dimension; 8 experts per pass.
+__global__ void __launch_bounds__(256) router_logits_f32(RouterLogitsParams p) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= p.T) return;
+  const float* x = static_cast<const float*>(p.x) + warp * p.ldx;
+  const float* w = static_cast<const float*>(p.w);
+  for (int e0 = 0; e0 < p.E1; e0 += 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int h = lane; h < p.H; h += 32) {
+      const float xv = x[h];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (e0 + j < p.E1) acc[j] = fmaf(xv, w[static_cast<int64_t>(e0 + j) * p.H + h], acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    }
+    if (lane < 8 && e0 + lane < p.E1) {
+      float v = acc[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j)
+        if (lane == j) v = acc[j];
+      if (p.bias) v += p.bias[e0 + lane];
+      p.logits[static_cast<int64_t>(warp) * p.E1 + e0 + lane] = v;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ selection
+constexpr int RS_MAXJ = 8;  // up to 256 routed experts
+
+__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+__global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
+  extern __shared__ int32_t hist[];  // [num_slots]
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) hist[s] = 0;
+  __syncthreads();
+
+  const int t_begin = blockIdx.x * p.tb;
+  const int t_end = min(p.T, t_begin + p.tb);
+  for (int t = t_begin + warp; t < t_end; t += blockDim.x >> 5) {
+    const float* lg = p.logits + static_cast<int64_t>(t) * p.E1;
+    float v[RS_MAXJ];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < RS_MAXJ; ++j) {
+      const int e = lane + 32 * j;
+      v[j] = (e < p.E) ? lg[e] : -INFINITY;
+      m = fmaxf(m, v[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < RS_MAXJ; ++j) {
+      const int e = lane + 32 * j;
+      v[j] = (e < p.E) ? expf(v[j] - m) : 0.f;
+      s += v[j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+#pragma unroll
+    for (int j = 0; j < RS_MAXJ; ++j) v[j] = (lane + 32 * j < p.E) ? v[j] / s : -1.f;
+
+    // top-k: K rounds of a warp arg-max on (prob desc, expert asc).
+    float selp[8];
+    int sele[8];
+    uint32_t taken = 0;
+    for (int k = 0; k < p.K; ++k) {
+      float bv = -2.f;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < RS_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        if (e < p.E && !((taken >> j) & 1u) && better(v[j], e, bv, bi)) {
+          bv = v[j];
+          bi = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      selp[k] = bv;
+      sele[k] = bi;
+    }
+    float denom = 1.f;
+    if (p.renorm) {
+      denom = 0.f;
+      for (int k = 0; k < p.K; ++k) denom += selp[k];
+    }
+    if (lane < p.K) {
+      float wk = 0.f;
+      int ek = 0;
+      for (int k = 0; k < p.K; ++k)
+        if (k == lane) {
+          wk = selp[k];
+          ek = sele[k];
+        }
+      if (p.renorm) wk = wk / denom;
+      wk *= p.scale;
+      if (p.round_bf16) wk = bf16_round(wk);
+      const int64_t flat = static_cast<int64_t>(t) * p.K + lane;
+      int phys = ek;
+      if (p.log2phy) {
+        const int rc = p.rep_count[ek];
+        const int r = (rc > 0) ? static_cast<int>(flat % rc) : 0;
+        phys = p.log2phy[ek * p.max_rep + r];
+      }
+      if (phys < 0 || phys >= p.num_slots) {
+        record_status(p.status, kStatusBadIndex);
+        phys = 0;
+      }
+      p.topk_ids[flat] = ek;
+      p.topk_w[flat] = wk;
+      p.phys_ids[flat] = phys;
+      atomicAdd(&hist[phys], 1);
+    }
+    if (p.has_shared_gate && lane == 0) {
+      const float g = lg[p.E];
+      p.shared_gate[t] = 1.f / (1.f + expf(-g));
+    }
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x)
+    p.block_counts[static_cast<int64_t>(s) * p.nblocks + blockIdx.x] = hist[s];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(p.ticket, 1u) == static_cast<uint32_t>(p.nblocks - 1));
+  __syncthreads();
+  if (!s_last) return;
+
+  // ---- last CTA: slot totals, slot offsets, absolute per-(slot, block) offsets.
+  __threadfence();
+  const int nb = p.nblocks;
+  const int per_lane = (nb + 31) / 32;
+  for (int s = warp; s < p.num_slots; s += blockDim.x >> 5) {
+    const int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
+    int part = 0;
+    for (int i = 0; i < per_lane; ++i) {
+      const int b = lane * per_lane + i;
+      if (b < nb) part += __ldcg(col + b);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane == 0) hist[s] = part;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int run = 0;
+    for (int base = 0; base < p.num_slots; base += 32) {
+      const int s = base + lane;
+      const int c = (s < p.num_slots) ? hist[s] : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      if (s < p.num_slots) {
+        p.slot_counts[s] = c;
+        p.slot_offsets[s] = run + incl - c;
+      }
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) p.slot_offsets[p.num_slots] = run;
+  }
+  __syncthreads();
+  for (int s = warp; s < p.num_slots; s += blockDim.x >> 5) {
+    int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
+    int part = 0;
+    for (int i = 0; i < per_lane; ++i) {
+      const int b = lane * per_lane + i;
+      if (b < nb) part += __ldcg(col + b);
+    }
+    int incl = part;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    int run = __ldcg(p.slot_offsets + s) + incl - part;
+    for (int i = 0; i < per_lane; ++i) {
+      const int b = lane * per_lane + i;
+      if (b < nb) {
+        const int c = __ldcg(col + b);
+        col[b] = run;
+        run += c;
+      }
+    }
+  }
+  if (threadIdx.x == 0) *p.ticket = 0u;
+}
+
+// ------------------------------------------------------------------ host launchers
+int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t stream) {
+  if (p.T == 0) return 0;
+  if (x_dtype == kDtypeBF16) {
+    const int tok_blocks = (p.T + RL_TOK - 1) / RL_TOK;
+    // Enough CTAs to cover the SMs: narrow column groups when the token count is small.
+    int cols = RL_MAXNT * 8;
+    while (cols > 8 && tok_blocks * ((p.E1 + cols - 1) / cols) < 2 * num_sms()) cols -= 8;
+    dim3 grid(tok_blocks, (p.E1 + cols - 1) / cols);
+    const size_t smem = static_cast<size_t>(RL_TOK + cols) * RL_LD * sizeof(__nv_bfloat16);
+    router_logits_bf16<<<grid, 128, smem, stream>>>(p, cols);
+  } else {
+    const int grid = (p.T * 32 + 255) / 256;
+    router_logits_f32<<<grid, 256, 0, stream>>>(p);
+  }
+  return 0;
+}
+
+int launch_router_select(const RouterSelectParams& p, cudaStream_t stream) {
+  if (p.T == 0) return 0;
+  const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t);
+  router_select<<<p.nblocks, 256, smem, stream>>>(p);
+  return 0;
+}
+
+}  // namespace b200moe

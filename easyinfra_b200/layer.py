@@ -1,0 +1,227 @@
+"""One expert-parallel MoE layer forward on the B200 kernels.
+
+The stages follow EasyInfra's all-to-all MoE block (MoeAll2AllBlock,
+easyinfra/generation/blocks/moe/moe_all2all.py):
+
+  ROUTING_DISPATCH  router + replica pick + histogram (kernel 1), permute (kernel 2),
+                    count all-gather and token all-to-all (NCCL)          :325-459
+  MOE               grouped SwiGLU GEMM + grouped down GEMM (kernel 3)    :523-558
+                    combine all-to-all (NCCL)                             :560-591
+  GATHER            weighted unpermute + shared expert add (kernel 4)     :593-604
+  SHARED_EXPERT     dense SwiGLU on the layer input (kernel 3 with P=1)   :461-521
+
+With one rank (G == 1) the whole layer runs without a host synchronisation: the
+router's last CTA writes the per-expert row offsets the grouped GEMMs read.  With
+G > 1 the layer synchronises once, after the count all-gather, exactly where the
+reference does (moe_all2all.py:410-424), because NCCL's all_to_all_single takes host
+split lists.  The received rows ([source rank][local slot] order) are regrouped into
+expert-major order by one gather kernel that also records the inverse row map; the
+down GEMM scatters its output rows straight back to received order, ready for the
+combine all-to-all.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .placement import Placement
+
+
+@dataclass
+class LayerParams:
+    """Weights of one MoE layer held by one rank (P physical slots)."""
+    gate_w: torch.Tensor                 # [E(+1), H]
+    w_gate_up: torch.Tensor              # [P, 2I, H] bf16
+    w_down: torch.Tensor                 # [P, H, I] bf16
+    gate_bias: Optional[torch.Tensor] = None     # [E(+1)] fp32
+    shared_gate_up: Optional[torch.Tensor] = None  # [2Is, H]
+    shared_down: Optional[torch.Tensor] = None     # [H, Is]
+
+
+@dataclass
+class DispatchState:
+    """What ROUTING_DISPATCH leaves for the later stages (one rank, one chunk)."""
+    T: int
+    route: ops.RouterOutput
+    perm: ops.PermuteOutput
+    send_splits: Optional[List[int]] = None    # rows to each destination rank
+    recv_splits: Optional[List[int]] = None    # rows from each source rank
+    recv: Optional[torch.Tensor] = None        # received rows [src][local slot]
+    expert_offsets: Optional[torch.Tensor] = None  # [P+1] expert-major row offsets (device)
+    seg_src: Optional[torch.Tensor] = None
+    seg_dst: Optional[torch.Tensor] = None
+    seg_len: Optional[torch.Tensor] = None
+    max_seg: int = 0
+    shared_out: Optional[torch.Tensor] = None
+
+
+class MoELayer:
+    """The MoE layer of one rank.  `placement` maps physical slots to logical experts
+    (rank-major, P slots per rank); `rank`/`group` select this rank's slots and the
+    torch.distributed process group used for the two all-to-alls (None for G == 1)."""
+
+    def __init__(self, params: LayerParams, placement: Placement, top_k: int, norm_topk_prob: bool,
+                 rank: int = 0, group=None, routed_scaling_factor: float = 1.0,
+                 shared_gate: bool = False, status: Optional[torch.Tensor] = None):
+        self.p = params
+        self.placement = placement
+        self.top_k = top_k
+        self.norm_topk_prob = norm_topk_prob
+        self.rank = rank
+        self.group = group
+        self.scale = routed_scaling_factor
+        self.shared_gate = shared_gate
+        self.G, self.P = placement.ep_size, placement.slots_per_rank
+        self.E = placement.num_logical
+        self.H = params.w_gate_up.shape[2]
+        self.I = params.w_gate_up.shape[1] // 2
+        dev = params.w_gate_up.device
+        self.device = dev
+        self.log2phy, self.rep_count = placement.device_tables(dev)
+        self.use_map = not placement.is_identity
+        self.ws = ops.Workspace(dev)
+        self.status = status
+        self._shared_offsets = {}
+        if params.gate_w.shape[0] != self.E + (1 if shared_gate else 0):
+            raise ValueError("gate_w rows must be E (+1 with a shared-expert gate)")
+
+    # ------------------------------------------------------------ ROUTING_DISPATCH
+    def route_and_permute(self, x: torch.Tensor) -> DispatchState:
+        T = x.shape[0]
+        E1 = self.p.gate_w.shape[0]
+        r = ops.router(x, self.p.gate_w, self.top_k, renorm=self.norm_topk_prob,
+                       gate_bias=self.p.gate_bias, scale=self.scale,
+                       has_shared_gate=self.shared_gate,
+                       log2phy=self.log2phy if self.use_map else None,
+                       rep_count=self.rep_count if self.use_map else None,
+                       num_slots=self.G * self.P, workspace=self.ws, status=self.status)
+        perm = ops.permute(x, r, num_slots=self.G * self.P, E1=E1)
+        return DispatchState(T=T, route=r, perm=perm)
+
+    def exchange_counts(self, st: DispatchState) -> np.ndarray:
+        """All-gather of per-slot counts ([G src, G*P] int32) and the one host sync
+        of the layer (moe_all2all.py:97-115, :410-424)."""
+        gathered = torch.empty(self.G, self.G * self.P, dtype=torch.int32, device=self.device)
+        dist.all_gather_into_tensor(gathered, st.route.slot_counts, group=self.group)
+        return gathered.cpu().numpy()
+
+    def plan_exchange(self, st: DispatchState, counts: np.ndarray) -> None:
+        """Host split lists and the regroup tables from the gathered counts."""
+        G, P, r = self.G, self.P, self.rank
+        c = counts.reshape(G, G, P)            # [src, dst, local slot]
+        st.send_splits = c[r].sum(-1).tolist()
+        mine = c[:, r, :]                      # [src, local slot] rows this rank receives
+        st.recv_splits = mine.sum(-1).tolist()
+        seg_start_recv = (np.cumsum(mine.reshape(-1)) - mine.reshape(-1)).reshape(G, P)
+        per_slot = mine.sum(0)                 # rows per local slot
+        offs = np.zeros(P + 1, dtype=np.int64)
+        offs[1:] = np.cumsum(per_slot)
+        dst = np.empty((P, G), dtype=np.int64)
+        for e in range(P):
+            dst[e] = offs[e] + np.cumsum(mine[:, e]) - mine[:, e]
+        src = seg_start_recv.T                 # [P, G]
+        ln = mine.T                            # [P, G]
+        table = np.concatenate([offs, src.reshape(-1), dst.reshape(-1), ln.reshape(-1)]).astype(np.int32)
+        dev_table = torch.from_numpy(table).pin_memory().to(self.device, non_blocking=True)
+        st.expert_offsets = dev_table[:P + 1]
+        st.seg_src = dev_table[P + 1:P + 1 + P * G]
+        st.seg_dst = dev_table[P + 1 + P * G:P + 1 + 2 * P * G]
+        st.seg_len = dev_table[P + 1 + 2 * P * G:]
+        st.max_seg = int(ln.max()) if ln.size else 0
+
+    def dispatch(self, st: DispatchState) -> None:
+        rows = int(sum(st.recv_splits))
+        st.recv = torch.empty(rows, self.H, dtype=st.perm.send.dtype, device=self.device)
+        dist.all_to_all_single(st.recv, st.perm.send, st.recv_splits, st.send_splits, group=self.group)
+
+    # ------------------------------------------------------------ SHARED_EXPERT
+    def shared_expert(self, x: torch.Tensor, st: DispatchState) -> None:
+        if self.p.shared_gate_up is None:
+            return
+        T = x.shape[0]
+        offs = self._shared_offsets.get(T)
+        if offs is None:
+            offs = torch.tensor([0, T], dtype=torch.int32, device=self.device)
+            self._shared_offsets[T] = offs
+        act = ops.grouped_swiglu(x, offs, self.p.shared_gate_up[None], status=self.status)
+        st.shared_out = ops.grouped_down(act, offs, self.p.shared_down[None], status=self.status)
+
+    # ------------------------------------------------------------ MOE
+    def experts_local(self, st: DispatchState) -> torch.Tensor:
+        """G == 1: the send buffer is already expert-major; offsets come from the router."""
+        send = st.perm.send
+        act = ops.grouped_swiglu(send, st.route.slot_offsets, self.p.w_gate_up, status=self.status)
+        return ops.grouped_down(act, st.route.slot_offsets, self.p.w_down, status=self.status)
+
+    def experts_ep(self, st: DispatchState) -> torch.Tensor:
+        """G > 1: regroup received rows to expert-major, run both GEMMs, and scatter the
+        down-projection rows back to received order."""
+        rows = st.recv.shape[0]
+        xe = torch.empty_like(st.recv)
+        row_map = torch.empty(rows, dtype=torch.int32, device=self.device)
+        ops.gather_segments(st.recv, xe, st.seg_src, st.seg_dst, st.seg_len, st.max_seg,
+                            inverse_map=row_map)
+        act = ops.grouped_swiglu(xe, st.expert_offsets, self.p.w_gate_up, status=self.status)
+        return ops.grouped_down(act, st.expert_offsets, self.p.w_down, out_row_map=row_map,
+                                status=self.status)
+
+    def combine_exchange(self, st: DispatchState, y_recv: torch.Tensor) -> torch.Tensor:
+        back = torch.empty(int(sum(st.send_splits)), self.H, dtype=y_recv.dtype, device=self.device)
+        dist.all_to_all_single(back, y_recv, st.send_splits, st.recv_splits, group=self.group)
+        return back
+
+    # ------------------------------------------------------------ GATHER
+    def unpermute(self, st: DispatchState, y_sorted: torch.Tensor,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return ops.combine(y_sorted, st.perm.pos_of, st.route.topk_weights, shared=st.shared_out,
+                           shared_gate=st.route.shared_gate, out=out)
+
+    # ------------------------------------------------------------ whole layer
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Routed output plus the (gated) shared-expert output for this rank's tokens."""
+        st = self.route_and_permute(x)
+        self.shared_expert(x, st)
+        if self.G == 1:
+            y = self.experts_local(st)
+            return self.unpermute(st, y, out)
+        counts = self.exchange_counts(st)
+        self.plan_exchange(st, counts)
+        self.dispatch(st)
+        y_recv = self.experts_ep(st)
+        back = self.combine_exchange(st, y_recv)
+        return self.unpermute(st, back, out)
+
+
+def forward_ep_single_device(layers: List[MoELayer], xs: List[torch.Tensor],
+                             return_states: bool = False):
+    """Run the G ranks of an expert-parallel layer on one device, in stage order,
+    with the count all-gather and both all-to-alls done as local row copies.  Every
+    kernel and every host-side table is the one the multi-process path uses; only the
+    transport differs.  Used to check the EP data path on a single GPU."""
+    G = len(layers)
+    sts = [l.route_and_permute(x) for l, x in zip(layers, xs)]
+    for l, x, st in zip(layers, xs, sts):
+        l.shared_expert(x, st)
+    counts = torch.stack([st.route.slot_counts for st in sts]).cpu().numpy()
+    for l, st in zip(layers, sts):
+        l.plan_exchange(st, counts)
+    for r, st in enumerate(sts):
+        parts = []
+        for s in range(G):
+            a = sum(sts[s].send_splits[:r])
+            parts.append(sts[s].perm.send[a:a + sts[s].send_splits[r]])
+        st.recv = torch.cat(parts, 0)
+    ys = [l.experts_ep(st) for l, st in zip(layers, sts)]
+    outs = []
+    for r, (l, st) in enumerate(zip(layers, sts)):
+        parts = []
+        for d in range(G):
+            a = sum(sts[d].recv_splits[:r])
+            parts.append(ys[d][a:a + sts[d].recv_splits[r]])
+        outs.append(l.unpermute(st, torch.cat(parts, 0)))
+    return (outs, sts) if return_states else outs

@@ -1,0 +1,186 @@
+/*
+ * b200moe — C ABI of the B200 (sm_100a) expert-parallel MoE layer forward.
+ *
+ * One shared library, libb200moe.so, exports the hot path of EasyInfra's
+ * all-to-all MoE block as plain C entry points: device pointers, sizes and a CUDA
+ * stream, no framework types.  Host code (the Python package easyinfra_b200, or a
+ * ctypes stub inside EasyInfra itself) owns every buffer; no entry point allocates
+ * device memory.  Every call is asynchronous on the given stream and returns 0 on
+ * success or a negative B200MOE_E* code; b200moe_last_error() describes the last
+ * failure of the calling thread.  Conditions that only the device can see (an
+ * out-of-range index, a bounded wait that timed out) are recorded in an optional
+ * caller-owned device status word (int32, zero == fine) that the caller reads at its
+ * next synchronisation point.
+ *
+ * Layout conventions (all row-major):
+ *   x            [T, H]       activations, bf16 (B200MOE_DTYPE_BF16) or fp32
+ *   gate_w       [E(+1), H]   router weight (row E = shared-expert gate, optional)
+ *   w_gate_up    [P, 2I, H]   bf16, gate rows 0..I-1 then up rows I..2I-1
+ *   w_down       [P, H, I]    bf16
+ *   phys ids     slot s of rank g is s = g * P + local slot (rank-major)
+ *
+ * The reference interface each entry point replaces is cited per function
+ * (paths relative to the EasyInfra repository).
+ */
+#ifndef B200MOE_H_
+#define B200MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200MOE_API __attribute__((visibility("default")))
+#else
+#define B200MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200MOE_ABI_VERSION 1
+
+#define B200MOE_OK 0
+#define B200MOE_EINVAL (-1)       /* bad argument (null pointer, size, alignment) */
+#define B200MOE_ECUDA (-2)        /* CUDA runtime/driver error */
+#define B200MOE_EUNSUPPORTED (-3) /* shape or dtype outside what the kernels cover */
+#define B200MOE_ENODEVICE (-4)    /* no sm_100 device current */
+
+#define B200MOE_DTYPE_BF16 0
+#define B200MOE_DTYPE_F32 1
+
+/* Device status word values (written by kernels, read by the caller). */
+#define B200MOE_STATUS_OK 0
+#define B200MOE_STATUS_TIMEOUT 1
+#define B200MOE_STATUS_CAPACITY 2
+#define B200MOE_STATUS_BAD_INDEX 3
+
+/* ABI version of the loaded library (B200MOE_ABI_VERSION it was built with). */
+B200MOE_API int b200moe_abi_version(void);
+
+/* Human-readable description of the calling thread's last failed call. */
+B200MOE_API const char* b200moe_last_error(void);
+
+/* Tokens per router/permute CTA for a chunk of T tokens (the two calls must agree;
+ * both derive it from T). */
+B200MOE_API int b200moe_tokens_per_block(int T);
+
+/* Bytes of workspace b200moe_router / b200moe_permute need for T tokens, E1 router
+ * columns and num_slots physical slots.  The first 256 bytes hold a completion
+ * counter that must be zero before the first call on a workspace; every call leaves
+ * it zero again, so zero the workspace once at allocation. */
+B200MOE_API size_t b200moe_router_workspace_bytes(int T, int E1, int num_slots);
+
+/*
+ * Router: logits, fp32 softmax, top-k (ties -> lowest expert id), optional renorm,
+ * scaling, rounding to the activation dtype, EPLB replica pick and slot histogram.
+ * Replaces Qwen3MoeSparseMoeBlock._routing (easyinfra/models/qwen3_moe/
+ * modeling_qwen3_moe.py:255-266) + eplb_map_to_physical_and_record
+ * (easyinfra/generation/blocks/moe/base.py:40-64) + _MoeBlock._all_expert_count_compute
+ * (base.py:343-364).
+ *
+ *   x, ldx, x_dtype   [T, H] activations (ldx in elements, 16-byte aligned rows)
+ *   gate_w            [E + has_shared_gate, H] same dtype as x
+ *   gate_bias         [E + has_shared_gate] fp32 logit bias or NULL
+ *   renorm            norm_topk_prob; scale: routed scaling factor (1.0 = none)
+ *   log2phy           [E, max_rep] int32 physical slot per (logical expert, replica)
+ *   rep_count         [E] int32 replica count; both NULL -> physical id = logical id
+ *   num_slots         G * P physical slots over all ranks
+ * Outputs (device): topk_ids [T,K] int32 logical ids, topk_w [T,K] fp32 (already
+ * rounded to the activation dtype), phys_ids [T,K] int32, shared_gate [T] fp32
+ * sigmoid of the shared-gate logit (only when has_shared_gate), slot_counts
+ * [num_slots] int32, slot_offsets [num_slots+1] int32 (exclusive prefix; entry
+ * num_slots == T*K).  logits_out [T, E1] fp32 may be NULL; when given, the logits
+ * (bf16-rounded for bf16 x) are kept there.
+ */
+B200MOE_API int b200moe_router(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
+                   const float* gate_bias, int has_shared_gate, int T, int H, int E, int K,
+                   int renorm, float scale, const int32_t* log2phy, const int32_t* rep_count,
+                   int max_rep, int num_slots, int32_t* topk_ids, float* topk_w,
+                   int32_t* phys_ids, float* shared_gate, int32_t* slot_counts,
+                   int32_t* slot_offsets, float* logits_out, void* workspace,
+                   size_t workspace_bytes, int* status, void* stream);
+
+/*
+ * The selection half of b200moe_router on caller-provided logits [T, E1] (fp32,
+ * holding bf16-rounded values for a bf16 model).  Used to pin the selection against
+ * the reference's own logits bit for bit.  round_bf16 rounds the final weights to
+ * bf16 (x.dtype == bfloat16 in the reference).
+ */
+B200MOE_API int b200moe_router_from_logits(const float* logits, int has_shared_gate, int T, int E, int K,
+                               int renorm, float scale, int round_bf16, const int32_t* log2phy,
+                               const int32_t* rep_count, int max_rep, int num_slots,
+                               int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                               float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets,
+                               void* workspace, size_t workspace_bytes, int* status,
+                               void* stream);
+
+/*
+ * Permute: writes every (token, k) row of x into send [T*K, H] in the order
+ * (physical slot, flat index t*K+k) — the reference's stable sort of the physical
+ * ids followed by x[send_indices] (easyinfra/generation/blocks/moe/
+ * moe_all2all.py:345-351).  Needs the workspace of the b200moe_router call that
+ * produced phys_ids (same T, E1, num_slots).  pos_of [T,K] int32 receives the send row
+ * of each (t, k); send_token / send_slot [T*K] int64 (nullable) receive the
+ * reference's send_indices and send_weight_top_k.
+ */
+B200MOE_API int b200moe_permute(const void* x, int64_t ldx, int x_dtype, int T, int H, int K, int E1,
+                    const int32_t* phys_ids, int num_slots, void* send, int32_t* pos_of,
+                    int64_t* send_token, int64_t* send_slot, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/*
+ * Grouped gate/up GEMM with SwiGLU: act[r, :] = silu(x[r] Wg_e^T) * (x[r] Wu_e^T) for
+ * every row r of expert e, rows of expert e being [offsets[e], offsets[e+1]) of x
+ * (expert-major).  bf16 in/out, fp32 accumulation, one rounding.  rows_cap is the
+ * allocated row count of x and act (>= offsets[P]).
+ * Replaces the gate_up projection + act_fn(gate) * up of NativeMoE / TritonExperts
+ * (easyinfra/generation/modules/moe/native_moe.py:56-103, base.py:39-42,
+ * fused_moe.py:443-459).
+ */
+B200MOE_API int b200moe_grouped_swiglu(const void* x, int64_t ldx, int64_t rows_cap,
+                           const int32_t* expert_offsets, int P, int H, int I,
+                           const void* w_gate_up, void* act, int64_t ld_act, int* status,
+                           void* stream);
+
+/*
+ * Grouped down GEMM: out[map(r), :] = act[r] Wd_e^T (map = identity when out_row_map is
+ * NULL).  Replaces the down projection of NativeMoE / TritonExperts
+ * (native_moe.py:56-103, fused_moe.py:462-476).
+ */
+B200MOE_API int b200moe_grouped_down(const void* act, int64_t ld_act, int64_t rows_cap,
+                         const int32_t* expert_offsets, int P, int H, int I,
+                         const void* w_down, void* out, int64_t ldo,
+                         const int32_t* out_row_map, int* status, void* stream);
+
+/*
+ * Combine / weighted unpermute: out[t] = sum_k topk_w[t,k] * y[pos_of[t,k]]
+ * (+ shared_gate[t] * shared[t] when shared != NULL; gate 1 when shared_gate == NULL),
+ * fp32 accumulation, one rounding to the output dtype.  Replaces
+ * MoeAll2AllBlock._all2all_chunk_output_compute (easyinfra/generation/blocks/moe/
+ * moe_all2all.py:291-307) and the shared-expert residual add (:536-537).
+ */
+B200MOE_API int b200moe_combine(const void* y, int64_t ldy, int dtype, const int32_t* pos_of,
+                    const float* topk_w, int T, int K, int H, const void* shared, int64_t lds,
+                    const float* shared_gate, void* out, int64_t ldo, void* stream);
+
+/*
+ * Row-segment gather used around the expert-parallel all-to-all: for each segment i,
+ * copies rows [src_start[i], src_start[i] + len[i]) of src to rows
+ * [dst_start[i], ...) of dst (row_bytes each, multiple of 16).  Segment tables are
+ * device int32 arrays; max_rows bounds every len[i].  dst_to_src (nullable, int32)
+ * receives, for every written dst row, the src row it came from.  Turns the received
+ * [source rank][local expert] layout (moe_all2all.py:441-444) into the expert-major
+ * layout the grouped GEMMs read; dst_to_src then serves as b200moe_grouped_down's
+ * out_row_map to write results back in received order.
+ */
+B200MOE_API int b200moe_gather_segments(const void* src, void* dst, int64_t row_bytes,
+                            const int32_t* src_start, const int32_t* dst_start,
+                            const int32_t* len, int nseg, int64_t max_rows,
+                            int32_t* dst_to_src, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MOE_H_ */

@@ -1,0 +1,56 @@
+"""The C-ABI library builds for sm_100a, loads, and exports every entry point that
+include/b200moe.h declares (no compute calls: no GPU needed)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+from easyinfra_b200 import _lib, build
+
+HEADER = os.path.join(build.REPO_DIR, "include", "b200moe.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"B200MOE_API\s+[\w\s\*]+?\b(b200moe_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "b200moe_router" in syms and "b200moe_grouped_swiglu" in syms
+    assert set(syms) == set(_lib.SIGNATURES), "ctypes table and header disagree"
+
+
+def test_library_builds_and_exports_all_symbols():
+    path = build.build()
+    lib = ctypes.CDLL(path)
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+
+
+def test_abi_version_and_host_only_queries():
+    lib = _lib.load()
+    assert lib.b200moe_abi_version() == 1
+    assert lib.b200moe_tokens_per_block(64) in (8, 16, 32)
+    ws = lib.b200moe_router_workspace_bytes(16384, 129, 160)
+    assert ws >= 256 + 16384 * 129 * 4
+
+
+def test_argument_errors_are_reported_without_a_gpu():
+    """Validation happens before any device call: bad sizes return B200MOE_E* codes."""
+    lib = _lib.load()
+    rc = lib.b200moe_router(None, 0, 0, None, None, 0, 1, 64, 0, 1, 0, 1.0, None, None, 0, 8,
+                            None, None, None, None, None, None, None, None, 0, None, None)
+    assert rc != 0
+    assert b"E=" in lib.b200moe_last_error()
+
+
+def test_no_cluster_shared_loads_in_sources():
+    """Code that runs on several GPUs must never issue a TMA/bulk load that fans out
+    to a whole cluster; the kernels' sources do not even name that form."""
+    needle = "multi" + "cast"
+    csrc = os.path.join(build.PKG_DIR, "csrc")
+    for f in os.listdir(csrc):
+        text = open(os.path.join(csrc, f)).read()
+        assert needle not in text, f

@@ -1,0 +1,234 @@
+"""Kernel parity on a B200 through the C ABI (marked gpu).
+
+Integer/index outputs (expert ids, physical slots, counts, offsets, permutation
+order, send rows) are compared bit-exactly with the CPU oracle.  Floating-point
+outputs use the north-star bound: max |a - b| / max |b| <= 1e-2 against the
+reference-dtype oracle, and a tighter bound against the oracle's fp32-accumulate
+mode (the numerics the kernels implement).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from easyinfra_b200 import configs as C
+from easyinfra_b200 import ops
+from oracle import moe_oracle as O
+from tests.conftest import load_golden
+from tests.golden import cases
+
+pytestmark = pytest.mark.gpu
+
+SPEC_TOL = 1e-2      # north-star bound vs the reference's own (bf16-chain) numerics
+TIGHT_TOL = 4e-3     # vs an unrounded fp32 result: one bf16 rounding is <= 2^-8 relative
+
+
+def max_rel(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def _routing_tables(case):
+    shape = case["shape"]
+    phy2log = cases.case_phy2log(case)
+    l2p, rep = O.log2phy_from_phy2log(phy2log, shape.num_experts)
+    return phy2log, l2p, rep
+
+
+@pytest.mark.parametrize("name", list(cases.CASES))
+def test_router_selection_bitexact_on_reference_logits(cuda_device, name):
+    """Selection kernel fed the reference's own logits: ids, physical slots, counts and
+    offsets bit-exact vs the oracle's canonical routing; weights within 1 ulp of the
+    activation dtype."""
+    case = cases.CASES[name]
+    g, _ = load_golden(name)
+    shape, G = case["shape"], case["G"]
+    phy2log, l2p, rep = _routing_tables(case)
+    use_map = case.get("use_eplb", False)
+    for r in range(G):
+        logits = torch.from_numpy(g[f"r{r}_logits"])
+        w_ref, ids_ref = O.route_from_logits(logits.to(shape.dtype), shape.top_k, shape.norm_topk_prob,
+                                             shape.dtype)
+        phys_ref = O.eplb_pick(ids_ref, l2p, rep) if use_map else ids_ref
+        counts_ref = O.slot_counts(phys_ref, G, phy2log.shape[1]).reshape(-1)
+        out = ops.router_from_logits(logits.to(cuda_device), shape.top_k, renorm=shape.norm_topk_prob,
+                                     round_bf16=shape.dtype == torch.bfloat16,
+                                     log2phy=l2p.to(cuda_device) if use_map else None,
+                                     rep_count=rep.to(cuda_device) if use_map else None,
+                                     num_slots=G * phy2log.shape[1])
+        torch.cuda.synchronize()
+        assert torch.equal(out.topk_ids.cpu().long(), ids_ref), (name, r)
+        assert torch.equal(out.phys_ids.cpu().long(), phys_ref), (name, r)
+        assert torch.equal(out.slot_counts.cpu().long(), counts_ref), (name, r)
+        offs = torch.zeros(counts_ref.numel() + 1, dtype=torch.long)
+        offs[1:] = counts_ref.cumsum(0)
+        assert torch.equal(out.slot_offsets.cpu().long(), offs), (name, r)
+        wk = out.topk_weights.cpu()
+        wr = w_ref.float()
+        if shape.dtype == torch.bfloat16:
+            ulp = wr.abs() * 2.0 ** -7
+            assert bool(((wk - wr).abs() <= ulp + 1e-30).all()), (name, r)
+        else:
+            assert float((wk - wr).abs().max()) <= 1e-6, (name, r)
+
+
+@pytest.mark.parametrize("name", list(cases.CASES))
+def test_router_logits_close_to_reference(cuda_device, name):
+    """Logit GEMM: bf16 logits equal the reference's except for rare 1-ulp rounding
+    differences from the fp32 accumulation order; fp32 logits within 1e-5."""
+    case = cases.CASES[name]
+    g, _ = load_golden(name)
+    shape = case["shape"]
+    gw = C.router_weight(shape, 0).to(cuda_device)
+    gb = C.gate_bias(shape, 0)
+    x = C.hidden_states(shape, case["T"], rank=0).to(cuda_device)
+    # the reference's gate bias is a parameter in the model dtype (BaseLinear)
+    out = ops.router(x, gw, shape.top_k, renorm=shape.norm_topk_prob,
+                     gate_bias=None if gb is None else gb.to(shape.dtype).float().to(cuda_device),
+                     has_shared_gate=shape.shared_gate, num_slots=shape.num_experts,
+                     keep_logits=True)
+    torch.cuda.synchronize()
+    got = out.logits.cpu()[:, :shape.num_experts]
+    ref = torch.from_numpy(g["r0_logits"])
+    if shape.dtype == torch.bfloat16:
+        diff = (got - ref).abs()
+        ulp = ref.abs().clamp_min(2.0 ** -100) * 2.0 ** -7
+        assert bool((diff <= ulp * 1.001 + 1e-6).all()), float(diff.max())
+        assert float((diff > 0).float().mean()) < 0.05
+    else:
+        assert float((got - ref).abs().max()) < 1e-5
+
+
+@pytest.mark.parametrize("name", list(cases.CASES))
+def test_permute_order_bitexact(cuda_device, name):
+    """Send rows, send_indices and send_weight_top_k equal the reference's stable sort
+    order; pos_of inverts it."""
+    case = cases.CASES[name]
+    g, _ = load_golden(name)
+    shape, G, T = case["shape"], case["G"], case["T"]
+    phy2log, l2p, rep = _routing_tables(case)
+    use_map = case.get("use_eplb", False)
+    logits = torch.from_numpy(g["r0_logits"])
+    _, ids_ref = O.route_from_logits(logits.to(shape.dtype), shape.top_k, shape.norm_topk_prob, shape.dtype)
+    phys_ref = O.eplb_pick(ids_ref, l2p, rep) if use_map else ids_ref
+    si, sk = O.permute_order(phys_ref, shape.top_k)
+    x = C.hidden_states(shape, T, rank=0)
+    r = ops.router_from_logits(logits.to(cuda_device), shape.top_k, renorm=shape.norm_topk_prob,
+                               round_bf16=shape.dtype == torch.bfloat16,
+                               log2phy=l2p.to(cuda_device) if use_map else None,
+                               rep_count=rep.to(cuda_device) if use_map else None,
+                               num_slots=G * phy2log.shape[1])
+    p = ops.permute(x.to(cuda_device), r, num_slots=G * phy2log.shape[1], E1=logits.shape[1],
+                    with_indices=True)
+    torch.cuda.synchronize()
+    assert torch.equal(p.send_token.cpu(), si)
+    assert torch.equal(p.send_slot.cpu(), sk)
+    assert torch.equal(p.send.cpu(), x[si])
+    pos = p.pos_of.cpu().long()
+    flat = torch.arange(T * shape.top_k)
+    inv = torch.empty_like(flat)
+    inv[si * shape.top_k + sk] = flat
+    assert torch.equal(pos.reshape(-1), inv)
+
+
+def _gemm_case(counts, H, I, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    P = len(counts)
+    rows = sum(counts)
+    x = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    wgu = (torch.randn(P, 2 * I, H, generator=g) * 0.05).to(torch.bfloat16)
+    wd = (torch.randn(P, H, I, generator=g) * 0.05).to(torch.bfloat16)
+    offs = torch.zeros(P + 1, dtype=torch.int32)
+    offs[1:] = torch.tensor(counts).cumsum(0)
+    return x, wgu, wd, offs
+
+
+def _gemm_ref(x, wgu, wd, offs):
+    """fp32 results before the final rounding: act (SwiGLU of GEMM1) and y (GEMM2 of
+    the bf16-rounded act, which is what the down kernel consumes)."""
+    P, twoI, _ = wgu.shape
+    I = twoI // 2
+    act = torch.zeros(x.shape[0], I, dtype=torch.float32)
+    y = torch.zeros(x.shape[0], wd.shape[1], dtype=torch.float32)
+    for e in range(P):
+        a, b = int(offs[e]), int(offs[e + 1])
+        if a == b:
+            continue
+        gu = x[a:b].float() @ wgu[e].float().T
+        h = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+        act[a:b] = h
+        y[a:b] = h.to(torch.bfloat16).float() @ wd[e].float().T
+    return act, y
+
+
+@pytest.mark.parametrize("counts,H,I", [
+    ([5], 256, 128),
+    ([128, 0, 129, 1], 256, 256),
+    ([300, 7, 0, 0, 64, 255], 512, 384),
+    ([1000, 17], 1024, 512),
+    ([0, 0, 3], 128, 64),
+])
+def test_grouped_gemms_match_fp32_reference(cuda_device, counts, H, I):
+    x, wgu, wd, offs = _gemm_case(counts, H, I, seed=sum(counts) + H + I, device=cuda_device)
+    act_ref, y_ref = _gemm_ref(x, wgu, wd, offs)
+    dx, doffs = x.to(cuda_device), offs.to(cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    act = ops.grouped_swiglu(dx, doffs, wgu.to(cuda_device), status=status)
+    y = ops.grouped_down(act_ref.to(torch.bfloat16).to(cuda_device), doffs, wd.to(cuda_device),
+                         status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert max_rel(act, act_ref) < TIGHT_TOL, max_rel(act, act_ref)
+    assert max_rel(y, y_ref) < TIGHT_TOL, max_rel(y, y_ref)
+
+
+def test_grouped_down_row_scatter(cuda_device):
+    counts, H, I = [70, 0, 200], 256, 128
+    x, wgu, wd, offs = _gemm_case(counts, H, I, seed=3, device=cuda_device)
+    act_ref, y_ref = _gemm_ref(x, wgu, wd, offs)
+    rows = sum(counts)
+    perm = torch.randperm(rows, generator=torch.Generator().manual_seed(5)).to(torch.int32)
+    y = ops.grouped_down(act_ref.to(torch.bfloat16).to(cuda_device), offs.to(cuda_device),
+                         wd.to(cuda_device), out_row_map=perm.to(cuda_device))
+    torch.cuda.synchronize()
+    expect = torch.empty_like(y_ref)
+    expect[perm.long()] = y_ref
+    assert max_rel(y, expect) < TIGHT_TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_combine_matches_fp32_reference(cuda_device, dtype):
+    g = torch.Generator().manual_seed(11)
+    T, K, H = 77, 6, 384
+    y = torch.randn(T * K, H, generator=g).to(dtype)
+    pos = torch.randperm(T * K, generator=g).view(T, K).to(torch.int32)
+    w = torch.rand(T, K, generator=g)
+    sh = torch.randn(T, H, generator=g).to(dtype)
+    sg = torch.rand(T, generator=g)
+    ref = (w[:, :, None] * y.float()[pos.long()]).sum(1) + sg[:, None] * sh.float()
+    out = ops.combine(y.to(cuda_device), pos.to(cuda_device), w.to(cuda_device),
+                      shared=sh.to(cuda_device), shared_gate=sg.to(cuda_device))
+    torch.cuda.synchronize()
+    tol = 4e-3 if dtype == torch.bfloat16 else 1e-6
+    assert max_rel(out, ref) < tol
+
+
+def test_gather_segments_and_inverse_map(cuda_device):
+    H = 64
+    src = torch.randn(50, H).to(torch.bfloat16)
+    s_start = torch.tensor([0, 10, 30, 45], dtype=torch.int32)
+    length = torch.tensor([10, 20, 15, 5], dtype=torch.int32)
+    d_start = torch.tensor([20, 0, 35, 30], dtype=torch.int32)
+    dst = torch.zeros(50, H, dtype=torch.bfloat16, device=cuda_device)
+    inv = torch.full((50,), -1, dtype=torch.int32, device=cuda_device)
+    ops.gather_segments(src.to(cuda_device), dst, s_start.to(cuda_device), d_start.to(cuda_device),
+                        length.to(cuda_device), int(length.max()), inverse_map=inv)
+    torch.cuda.synchronize()
+    expect = torch.empty_like(src)
+    inv_ref = torch.empty(50, dtype=torch.int32)
+    for a, b, n in zip(s_start.tolist(), d_start.tolist(), length.tolist()):
+        expect[b:b + n] = src[a:a + n]
+        inv_ref[b:b + n] = torch.arange(a, a + n, dtype=torch.int32)
+    assert torch.equal(dst.cpu(), expect)
+    assert torch.equal(inv.cpu(), inv_ref)
