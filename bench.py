@@ -199,7 +199,7 @@ def build_stack(cfg_key, rank, world, device, group, n_layers):
             sd = torch.randn(H, Is, generator=g, device=device, dtype=shape.dtype).mul_(0.02)
         params = LayerParams(gw, wgu, wd, None if gb is None else gb.to(shape.dtype).float().to(device),
                              sgu, sd)
-        layers.append(MoELayer(params, pl, shape.top_k, shape.norm_topk_prob, rank=rank, group=group,
+        layers.append(MoELayer(params, pl, shape.top_k, shape.norm_topk_prob, rank=rank, comm=group,
                                shared_gate=shape.shared_gate))
     return shape, layers
 
@@ -219,8 +219,9 @@ def run_ours(args):
     build.build()
     group = None
     if world > 1:
+        from easyinfra_b200.communicator import GroupCommunicator
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
-        group = dist.group.WORLD
+        group = GroupCommunicator(group=dist.group.WORLD)
     cfg_key, phase, tokens = WORKLOADS[args.workload]
     shape = C.CONFIGS[cfg_key]
     n_layers = args.layers or shape.num_layers

@@ -26,10 +26,35 @@ from typing import List, Optional
 
 import numpy as np
 import torch
-import torch.distributed as dist
 
 from . import ops
+from .communicator import GroupCommunicator
 from .placement import Placement
+
+
+def regroup_tables(mine: np.ndarray):
+    """Tables that turn received rows in [source rank][local slot] order (the layout
+    all_to_all_single produces, moe_all2all.py:441-444) into expert-major order.
+    mine[s, e] = rows from source s for local slot e.  Returns (expert_offsets [P+1],
+    seg_src [P*G], seg_dst [P*G], seg_len [P*G], max_seg) as int arrays; segment
+    (e, s) is listed at index e*G + s."""
+    G, P = mine.shape
+    flat = mine.reshape(-1)
+    seg_start_recv = (np.cumsum(flat) - flat).reshape(G, P)
+    offs = np.zeros(P + 1, dtype=np.int64)
+    offs[1:] = np.cumsum(mine.sum(0))
+    dst = offs[:P, None] + np.cumsum(mine.T, axis=1) - mine.T  # [P, G]
+    src = seg_start_recv.T
+    ln = mine.T
+    return offs, src.reshape(-1), dst.reshape(-1), ln.reshape(-1), int(ln.max()) if ln.size else 0
+
+
+def upload_tables(device, offs, src, dst, ln):
+    """One pinned host->device copy of the four tables; returns device views."""
+    P1, S = offs.size, src.size
+    table = np.concatenate([offs, src, dst, ln]).astype(np.int32)
+    dev = torch.from_numpy(table).pin_memory().to(device, non_blocking=True)
+    return dev[:P1], dev[P1:P1 + S], dev[P1 + S:P1 + 2 * S], dev[P1 + 2 * S:]
 
 
 @dataclass
@@ -62,18 +87,20 @@ class DispatchState:
 
 class MoELayer:
     """The MoE layer of one rank.  `placement` maps physical slots to logical experts
-    (rank-major, P slots per rank); `rank`/`group` select this rank's slots and the
-    torch.distributed process group used for the two all-to-alls (None for G == 1)."""
+    (rank-major, P slots per rank); `rank` selects this rank's slots and `comm` (an
+    expert-parallel GroupCommunicator) carries the count all-gather and the two
+    all-to-alls (None when G == 1 or when the caller moves the rows itself)."""
 
     def __init__(self, params: LayerParams, placement: Placement, top_k: int, norm_topk_prob: bool,
-                 rank: int = 0, group=None, routed_scaling_factor: float = 1.0,
-                 shared_gate: bool = False, status: Optional[torch.Tensor] = None):
+                 rank: int = 0, comm: Optional[GroupCommunicator] = None,
+                 routed_scaling_factor: float = 1.0, shared_gate: bool = False,
+                 status: Optional[torch.Tensor] = None):
         self.p = params
         self.placement = placement
         self.top_k = top_k
         self.norm_topk_prob = norm_topk_prob
         self.rank = rank
-        self.group = group
+        self.comm = comm
         self.scale = routed_scaling_factor
         self.shared_gate = shared_gate
         self.G, self.P = placement.ep_size, placement.slots_per_rank
@@ -106,9 +133,9 @@ class MoELayer:
     def exchange_counts(self, st: DispatchState) -> np.ndarray:
         """All-gather of per-slot counts ([G src, G*P] int32) and the one host sync
         of the layer (moe_all2all.py:97-115, :410-424)."""
-        gathered = torch.empty(self.G, self.G * self.P, dtype=torch.int32, device=self.device)
-        dist.all_gather_into_tensor(gathered, st.route.slot_counts, group=self.group)
-        return gathered.cpu().numpy()
+        gathered = torch.empty(self.G * self.G * self.P, dtype=torch.int32, device=self.device)
+        self.comm.all_gather_into_tensor(gathered, st.route.slot_counts).wait()
+        return gathered.view(self.G, self.G * self.P).cpu().numpy()
 
     def plan_exchange(self, st: DispatchState, counts: np.ndarray) -> None:
         """Host split lists and the regroup tables from the gathered counts."""
@@ -117,27 +144,13 @@ class MoELayer:
         st.send_splits = c[r].sum(-1).tolist()
         mine = c[:, r, :]                      # [src, local slot] rows this rank receives
         st.recv_splits = mine.sum(-1).tolist()
-        seg_start_recv = (np.cumsum(mine.reshape(-1)) - mine.reshape(-1)).reshape(G, P)
-        per_slot = mine.sum(0)                 # rows per local slot
-        offs = np.zeros(P + 1, dtype=np.int64)
-        offs[1:] = np.cumsum(per_slot)
-        dst = np.empty((P, G), dtype=np.int64)
-        for e in range(P):
-            dst[e] = offs[e] + np.cumsum(mine[:, e]) - mine[:, e]
-        src = seg_start_recv.T                 # [P, G]
-        ln = mine.T                            # [P, G]
-        table = np.concatenate([offs, src.reshape(-1), dst.reshape(-1), ln.reshape(-1)]).astype(np.int32)
-        dev_table = torch.from_numpy(table).pin_memory().to(self.device, non_blocking=True)
-        st.expert_offsets = dev_table[:P + 1]
-        st.seg_src = dev_table[P + 1:P + 1 + P * G]
-        st.seg_dst = dev_table[P + 1 + P * G:P + 1 + 2 * P * G]
-        st.seg_len = dev_table[P + 1 + 2 * P * G:]
-        st.max_seg = int(ln.max()) if ln.size else 0
+        offs, src, dst, ln, st.max_seg = regroup_tables(mine)
+        st.expert_offsets, st.seg_src, st.seg_dst, st.seg_len = upload_tables(self.device, offs, src, dst, ln)
 
     def dispatch(self, st: DispatchState) -> None:
         rows = int(sum(st.recv_splits))
         st.recv = torch.empty(rows, self.H, dtype=st.perm.send.dtype, device=self.device)
-        dist.all_to_all_single(st.recv, st.perm.send, st.recv_splits, st.send_splits, group=self.group)
+        self.comm.all_to_all_single(st.recv, st.perm.send, st.recv_splits, st.send_splits).wait()
 
     # ------------------------------------------------------------ SHARED_EXPERT
     def shared_expert(self, x: torch.Tensor, st: DispatchState) -> None:
@@ -172,7 +185,7 @@ class MoELayer:
 
     def combine_exchange(self, st: DispatchState, y_recv: torch.Tensor) -> torch.Tensor:
         back = torch.empty(int(sum(st.send_splits)), self.H, dtype=y_recv.dtype, device=self.device)
-        dist.all_to_all_single(back, y_recv, st.send_splits, st.recv_splits, group=self.group)
+        self.comm.all_to_all_single(back, y_recv, st.send_splits, st.recv_splits).wait()
         return back
 
     # ------------------------------------------------------------ GATHER

@@ -119,7 +119,13 @@ def router(x: torch.Tensor, gate_w: torch.Tensor, top_k: int, *, renorm: bool,
     ws_bytes = router_workspace_bytes(T, E1, num_slots)
     ws = (workspace or Workspace(dev)).get(ws_bytes)
     if gate_bias is not None:
-        gate_bias = gate_bias.to(torch.float32).contiguous()
+        # one fp32 bias per router column; the shared-expert gate column has none
+        gate_bias = gate_bias.to(torch.float32).reshape(-1)
+        if has_shared_gate and gate_bias.numel() == E:
+            gate_bias = torch.cat([gate_bias, gate_bias.new_zeros(1)])
+        if gate_bias.numel() != E1:
+            raise ValueError(f"gate_bias has {gate_bias.numel()} entries, router has {E1} columns")
+        gate_bias = gate_bias.contiguous()
     max_rep = 0
     if log2phy is not None:
         log2phy = log2phy.to(torch.int32).contiguous()

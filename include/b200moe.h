@@ -81,7 +81,8 @@ B200MOE_API size_t b200moe_router_workspace_bytes(int T, int E1, int num_slots);
  *
  *   x, ldx, x_dtype   [T, H] activations (ldx in elements, 16-byte aligned rows)
  *   gate_w            [E + has_shared_gate, H] same dtype as x
- *   gate_bias         [E + has_shared_gate] fp32 logit bias or NULL
+ *   gate_bias         [E + has_shared_gate] fp32 logit bias or NULL (exactly one entry
+ *                     per router column: the kernel reads E + has_shared_gate floats)
  *   renorm            norm_topk_prob; scale: routed scaling factor (1.0 = none)
  *   log2phy           [E, max_rep] int32 physical slot per (logical expert, replica)
  *   rep_count         [E] int32 replica count; both NULL -> physical id = logical id
