@@ -35,6 +35,12 @@ SIGNATURES = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_size_t, c_void_p, c_void_p],
     ),
+    "b200moe_router_noalloc": (
+        c_int,
+        [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_float, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    ),
     "b200moe_router_from_logits": (
         c_int,
         [c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_void_p, c_void_p,

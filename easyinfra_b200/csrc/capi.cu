@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/b200moe.h"
 #include "kernels.cuh"
@@ -409,3 +410,67 @@ int b200moe_gather_segments(const void* src, void* dst, int64_t row_bytes,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ allocation-free router
+// Scratch of b200moe_router_noalloc: one file-scope device array.  Every GPU on which
+// this library is loaded holds these bytes until the process exits.  Calls share it
+// and it keeps the last call's contents, so calls that overlap on the GPU race.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+}  // namespace
+
+static __device__ __align__(256) uint8_t g_router_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {nullptr};
+
+// Device address of g_router_scratch on the current device.  Looked up once per
+// device (with that device current), on the first call there.  In host code the
+// symbol itself is only a host-side stand-in, never a device address.
+int router_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(B200MOE_ENODEVICE, "no usable current CUDA device");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(B200MOE_ECUDA, "cudaGetSymbolAddress(router scratch) on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return B200MOE_OK;
+}
+
+}  // namespace
+
+extern "C" int b200moe_router_noalloc(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
+                                      const float* gate_bias, int has_shared_gate, int T, int H, int E,
+                                      int K, int renorm, float scale, const int32_t* log2phy,
+                                      const int32_t* rep_count, int max_rep, int num_slots,
+                                      int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                                      float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets,
+                                      float* logits_out, int* status, void* stream) {
+  if (T < 0 || E < 1 || num_slots < 1) return fail(B200MOE_EINVAL, "T=%d E=%d num_slots=%d", T, E, num_slots);
+  const int E1 = E + (has_shared_gate ? 1 : 0);
+  const size_t need = router_ws_layout(nullptr, T, E1, num_slots).bytes;
+  if (need > kNoAllocScratchBytes)
+    return fail(B200MOE_EUNSUPPORTED,
+                "b200moe_router_noalloc: T=%d, %d router columns and %d slots need %zu bytes of scratch; "
+                "the built-in scratch holds %zu bytes (use b200moe_router with a caller workspace)",
+                T, E1, num_slots, need, kNoAllocScratchBytes);
+  void* ws = nullptr;
+  int rc = router_scratch_address(&ws);
+  if (rc) return rc;
+  // The completion counter must read zero when the kernels start; a call that was cut
+  // short could have left it set, so clear it on the caller's stream every time.
+  const cudaError_t e = cudaMemsetAsync(ws, 0, kTicketBytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(B200MOE_ECUDA, "clearing the router scratch counter: %s", cudaGetErrorString(e));
+  return b200moe_router(x, ldx, x_dtype, gate_w, gate_bias, has_shared_gate, T, H, E, K, renorm, scale,
+                        log2phy, rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate,
+                        slot_counts, slot_offsets, logits_out, ws, kNoAllocScratchBytes, status, stream);
+}

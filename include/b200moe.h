@@ -103,6 +103,30 @@ B200MOE_API int b200moe_router(const void* x, int64_t ldx, int x_dtype, const vo
                    size_t workspace_bytes, int* status, void* stream);
 
 /*
+ * b200moe_router without a workspace argument: it allocates nothing and takes no
+ * caller scratch.  No counterpart in the reference (EasyInfra allocates everything
+ * through PyTorch).  For callers that cannot allocate device memory: a plugin handed
+ * only input/output device pointers by a host runtime that owns the allocator, or a
+ * caller on a latency path where a cudaMalloc (which can synchronise the device) is
+ * not acceptable.  The caller still passes every input and output.
+ * Scratch is a built-in device array of 8 MiB (ticket + per-block slot counts +
+ * logits), held by every GPU that loads the library until the process exits; calls
+ * needing more (see b200moe_router_workspace_bytes) return B200MOE_EUNSUPPORTED.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress), so
+ * make that first call before any stream capture.  All calls share the array and it
+ * keeps the last call's contents (each call clears the counter it needs zeroed first):
+ * calls that overlap on the GPU race, so serialise them (one stream, or events).
+ * It is not usable with b200moe_permute, which needs the workspace of its router call.
+ */
+B200MOE_API int b200moe_router_noalloc(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
+                                       const float* gate_bias, int has_shared_gate, int T, int H, int E,
+                                       int K, int renorm, float scale, const int32_t* log2phy,
+                                       const int32_t* rep_count, int max_rep, int num_slots,
+                                       int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                                       float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets,
+                                       float* logits_out, int* status, void* stream);
+
+/*
  * The selection half of b200moe_router on caller-provided logits [T, E1] (fp32,
  * holding bf16-rounded values for a bf16 model).  Used to pin the selection against
  * the reference's own logits bit for bit.  round_bf16 rounds the final weights to
