@@ -6,9 +6,10 @@ layer forward, one process per GPU.
 
 A step is one forward pass of the whole MoE stack of the workload (every layer with
 its own weights and placement) over one batch of synthetic tokens per rank:
-router -> permute -> dispatch all-to-all -> grouped SwiGLU + down GEMMs -> combine
-all-to-all -> weighted unpermute (+ shared expert where the model has one).  Layers
-are chained (layer l+1 consumes layer l's output).  Each rank serves its own batch
+residual add + RMSNorm -> router -> permute -> dispatch all-to-all -> grouped SwiGLU
++ down GEMMs -> combine all-to-all -> weighted unpermute (+ shared expert where the
+model has one).  Layers are chained through the residual stream as in the model
+(residual += hidden; hidden = MoE(RMSNorm(residual)); attention omitted).  Each rank serves its own batch
 (attention is data-parallel in the reference), so per-GPU work is fixed as N grows
 ("weak" scaling); value = tokens of all ranks x layers / max-over-ranks step time.
 
@@ -242,72 +243,80 @@ def run_ours(args):
     results = {}
 
     def measure(wl_name, with_roofline):
+        from easyinfra_b200.stack import MoEStack
         cfg_key_w, phase_w, T = WORKLOADS[wl_name]
         x = C.hidden_states(shape, T, rank=rank, device=device)
-        bufs = [torch.empty_like(x), torch.empty_like(x)]
-
-        def step(inp):
-            h = inp
-            for i, lay in enumerate(layers):
-                h = lay.forward(h, out=bufs[i % 2])
-            return h
-
+        stack = MoEStack(layers)
         for _ in range(args.warmup):
-            step(x)
+            stack.forward(x)
         torch.cuda.synchronize()
         # routing statistics of this input for the algorithmic roofline numbers
-        rows, hit = [], []
-        h = x
-        for i, lay in enumerate(layers):
-            st = lay.route_and_permute(h)
-            h = lay.forward(h, out=bufs[i % 2])
-            rows.append(st)
-        torch.cuda.synchronize()
         layer_rows, layer_hit = [], []
-        for lay, st in zip(layers, rows):
+        residual, hidden = x, None
+        for lay in layers:
+            residual, normed = ops.add_rmsnorm(residual, hidden, lay.p.norm_weight, lay.p.norm_eps)
+            st = lay.route_and_permute(normed)
+            hidden = lay.forward(normed)
             c = st.route.slot_counts.view(lay.G, lay.P).cpu()
-            if lay.G == 1:
-                layer_rows.append(int(c.sum()))
-                layer_hit.append(int((c[0] > 0).sum()))
-            else:
-                layer_rows.append(None)
-                layer_hit.append(None)
-        del rows
-        # device-timed region
+            layer_rows.append(int(c.sum()) if lay.G == 1 else None)
+            layer_hit.append(int((c[0] > 0).sum()) if lay.G == 1 else None)
+        torch.cuda.synchronize()
         ev = []
 
         def hook(name, ph):
             if name == "grouped_swiglu":
-                e = torch.cuda.Event(enable_timing=True)
+                e = torch.cuda.Event(enable_timing=True, external=True)
                 e.record()
                 ev.append(e)
 
+        ops.LAUNCHES["count"] = 0
+        if world == 1:
+            # one rank: the stack never syncs with the host -> one CUDA graph per step
+            def arm():
+                ops.LAUNCHES["count"] = 0   # count the captured forward only, not the warm-ups
+                if with_roofline:
+                    ops.EVENT_HOOK["fn"] = hook
+            graph = stack.capture(T, on_capture=arm)
+            ops.EVENT_HOOK["fn"] = None
+            launches_per_step = ops.LAUNCHES["count"]
+            graph.input.copy_(x)
+            run = lambda inp: graph(inp)  # noqa: E731
+            for _ in range(args.warmup):
+                run(x)
+        else:
+            run = stack.forward
+            launches_per_step = None
         sampler = ClockSampler(local_rank) if with_roofline else None
         barrier()
         torch.cuda.synchronize()
-        ops.LAUNCHES["count"] = 0
-        ops.EVENT_HOOK["fn"] = hook if with_roofline else None
+        if world > 1:
+            ops.LAUNCHES["count"] = 0
+            ops.EVENT_HOOK["fn"] = hook if with_roofline else None
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
         for _ in range(args.steps):
-            step(x)
+            run(x)
         t1.record()
         torch.cuda.synchronize()
         ops.EVENT_HOOK["fn"] = None
-        launches = ops.LAUNCHES["count"]
+        launches = launches_per_step * args.steps if launches_per_step is not None else ops.LAUNCHES["count"]
         barrier()
         clocks = sampler.stop() if sampler else None
         ms = t0.elapsed_time(t1) / args.steps
         ms = max_over_ranks(ms)
-        kernel_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev) - 1, 2)]
+        kernel_ms = []
+        try:
+            kernel_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev) - 1, 2)]
+        except RuntimeError:
+            kernel_ms = []
         # e2e: host buffers, H2D of the input and D2H of the result inside the region
         xh = x.cpu().pin_memory()
         oh = torch.empty_like(xh).pin_memory()
-        xd = torch.empty_like(x)
+        xd = graph.input if world == 1 else torch.empty_like(x)
         for _ in range(args.warmup):
             xd.copy_(xh, non_blocking=True)
-            oh.copy_(step(xd), non_blocking=True)
+            oh.copy_(run(xd), non_blocking=True)
         barrier()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -315,7 +324,7 @@ def run_ours(args):
         e0.record()
         for _ in range(args.steps):
             xd.copy_(xh, non_blocking=True)
-            oh.copy_(step(xd), non_blocking=True)
+            oh.copy_(run(xd), non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
         barrier()
@@ -324,7 +333,7 @@ def run_ours(args):
         res = {"workload": wl_name, "T": T, "ms": ms, "value": tok / (ms / 1e3),
                "e2e_value": tok / (e2e_ms / 1e3), "e2e_ms": e2e_ms,
                "h2d": xh.numel() * xh.element_size() * world, "d2h": oh.numel() * oh.element_size() * world,
-               "launches": launches // args.steps * args.steps, "clocks": clocks}
+               "launches": launches, "clocks": clocks, "graph": world == 1}
         if with_roofline and kernel_ms and layer_rows[0] is not None:
             # algorithmic work of the SwiGLU GEMM per launch, averaged over layers
             H, I = shape.hidden, shape.intermediate
@@ -342,7 +351,8 @@ def run_ours(args):
                 res["roofline"] = {"kernel": "grouped_swiglu", "bound": "hbm", "achieved": ach,
                                    "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                                    "peak_kind": f"{peak_kind} HBM copy",
-                                   "kernel_ms": per_launch_ms, "traffic": traffic_for(wl_name)}
+                                   "kernel_ms": per_launch_ms, "traffic": traffic_for(wl_name),
+                                   "hit_slots_mean": statistics.mean(layer_hit)}
         return res
 
     main = measure(args.workload, with_roofline=True)
@@ -351,7 +361,7 @@ def run_ours(args):
         for wl in SECONDARY.get(args.workload, []):
             if WORKLOADS[wl][0] == cfg_key:
                 s = measure(wl, with_roofline=True)
-                secondary.append({k: s[k] for k in ("workload", "value", "ms", "e2e_value") if k in s}
+                secondary.append({k: s[k] for k in ("workload", "value", "ms", "e2e_value", "graph") if k in s}
                                  | ({"roofline": s["roofline"]} if "roofline" in s else {}))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -376,6 +386,7 @@ def run_ours(args):
         "e2e": {"value": main["e2e_value"], "unit": UNIT, "h2d_bytes_per_step": main["h2d"],
                 "d2h_bytes_per_step": main["d2h"], "ms_per_step": main["e2e_ms"]},
         "gpu_launches": main["launches"],
+        "cuda_graph": main["graph"],
         "roofline": main.get("roofline"),
         "cpu_baseline": cpu,
         "clocks": main["clocks"],

@@ -35,6 +35,12 @@ SIGNATURES = {
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_size_t, c_void_p, c_void_p],
     ),
+    "b200moe_router_sigmoid_grouped": (
+        c_int,
+        [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_float, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p],
+    ),
     "b200moe_router_noalloc": (
         c_int,
         [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
@@ -62,10 +68,25 @@ SIGNATURES = {
         [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
          c_int64, c_void_p, c_void_p, c_void_p],
     ),
+    "b200moe_grouped_swiglu_f32": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int64,
+         c_void_p],
+    ),
+    "b200moe_grouped_down_f32": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int64,
+         c_void_p, c_void_p],
+    ),
     "b200moe_combine": (
         c_int,
         [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
          c_int64, c_void_p, c_void_p, c_int64, c_void_p],
+    ),
+    "b200moe_add_rmsnorm": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_int64, c_void_p, c_void_p,
+         c_int64, c_void_p],
     ),
     "b200moe_gather_segments": (
         c_int,

@@ -51,7 +51,8 @@ class _Linear(nn.Module):
 
 
 class _RMSNorm(nn.Module):
-    """_rmsnorm (easyinfra/generation/modules/rmsnorm/base_rmsnorm.py:6-12)."""
+    """Holds the post_attention_layernorm weight; the normalisation itself runs in the
+    fused add + RMSNorm kernel (_rmsnorm, generation/modules/rmsnorm/base_rmsnorm.py:6-12)."""
 
     def __init__(self, hidden, eps, dtype, device):
         super().__init__()
@@ -59,10 +60,7 @@ class _RMSNorm(nn.Module):
         self.variance_epsilon = eps
 
     def forward(self, t):
-        dt = t.dtype
-        f = t.to(torch.float32)
-        f = f * torch.rsqrt(f.pow(2).mean(-1, keepdim=True) + self.variance_epsilon)
-        return self.weight * f.to(dt)
+        return ops.add_rmsnorm(t, None, self.weight, self.variance_epsilon)[1]
 
 
 class B200MoeAll2AllBlock(nn.Module):
@@ -190,8 +188,11 @@ class B200MoeAll2AllBlock(nn.Module):
         residual, hidden_states = chunk.active_variables
         chunk.active_variables = ()
         T = residual.shape[-2]
-        residual = residual + hidden_states.view(-1, self.hidden_size)[:T]   # _add_to_residual
-        normed = self.post_attention_layernorm(residual).view(-1, self.hidden_size)
+        # _add_to_residual + post_attention_layernorm in one kernel
+        residual, normed = ops.add_rmsnorm(residual.view(-1, self.hidden_size),
+                                           hidden_states.view(-1, self.hidden_size)[:T],
+                                           self.post_attention_layernorm.weight,
+                                           self.post_attention_layernorm.variance_epsilon)
         st = self.layer().route_and_permute(normed)
         chunk.active_variables = (st, normed if self.has_shared else None, residual)
 

@@ -4,6 +4,7 @@
 // configurations and launches on the caller's stream.  It never allocates device
 // memory and never throws across the ABI.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -71,6 +72,17 @@ int check_launch(const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// B200MOE_GEMM_VARIANT=token|token_small|weight forces one grouped-GEMM kernel
+// (tuning and tests); unset or "auto" picks by rows per slot.
+int gemm_variant_from_env() {
+  const char* v = getenv("B200MOE_GEMM_VARIANT");
+  if (v == nullptr || strcmp(v, "auto") == 0) return kGemmAuto;
+  if (strcmp(v, "token") == 0) return kGemmTokenMajor;
+  if (strcmp(v, "token_small") == 0) return kGemmTokenMajorSmallM;
+  if (strcmp(v, "weight") == 0) return kGemmWeightMajor;
+  return kGemmAuto;
+}
+
 constexpr size_t kTicketBytes = 256;
 
 int tokens_per_block(int T) {
@@ -120,8 +132,13 @@ int select_common(const float* logits, int has_shared_gate, int T, int E, int K,
                   float scale, int round_bf16, const int32_t* log2phy, const int32_t* rep_count,
                   int max_rep, int num_slots, int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
                   float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets,
-                  const RouterWs& ws, int* status, cudaStream_t stream) {
+                  const RouterWs& ws, int* status, cudaStream_t stream, int scoring = 0,
+                  int n_group = 1, int topk_group = 1, const float* correction_bias = nullptr) {
   RouterSelectParams s;
+  s.scoring = scoring;
+  s.n_group = n_group;
+  s.topk_group = topk_group;
+  s.correction_bias = correction_bias;
   s.logits = logits;
   s.T = T;
   s.E = E;
@@ -163,9 +180,18 @@ int check_select_args(int T, int E, int K, int num_slots, const int32_t* log2phy
   if (log2phy == nullptr && num_slots < E)
     return fail(B200MOE_EINVAL, "num_slots=%d < E=%d without a placement map", num_slots, E);
   if (log2phy != nullptr && max_rep < 1) return fail(B200MOE_EINVAL, "max_rep=%d", max_rep);
-  if (!topk_ids || !topk_w || !phys_ids || !slot_counts || !slot_offsets)
-    return fail(B200MOE_EINVAL, "null output pointer");
-  if (has_shared_gate && !shared_gate) return fail(B200MOE_EINVAL, "shared_gate output is NULL");
+  if (!slot_counts || !slot_offsets) return fail(B200MOE_EINVAL, "null slot_counts/slot_offsets");
+  if (T > 0 && (!topk_ids || !topk_w || !phys_ids)) return fail(B200MOE_EINVAL, "null output pointer");
+  if (T > 0 && has_shared_gate && !shared_gate) return fail(B200MOE_EINVAL, "shared_gate output is NULL");
+  return B200MOE_OK;
+}
+
+// A chunk without tokens still reports (zero) counts and offsets: a rank with no
+// tokens takes part in the count exchange like any other.
+int zero_counts(int32_t* slot_counts, int32_t* slot_offsets, int num_slots, cudaStream_t stream) {
+  if (cudaMemsetAsync(slot_counts, 0, sizeof(int32_t) * num_slots, stream) != cudaSuccess ||
+      cudaMemsetAsync(slot_offsets, 0, sizeof(int32_t) * (num_slots + 1), stream) != cudaSuccess)
+    return fail(B200MOE_ECUDA, "zeroing slot counts: %s", cudaGetErrorString(cudaGetLastError()));
   return B200MOE_OK;
 }
 
@@ -197,6 +223,7 @@ int b200moe_router(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
   if ((rc = device_ok())) return rc;
   if (x_dtype != B200MOE_DTYPE_BF16 && x_dtype != B200MOE_DTYPE_F32)
     return fail(B200MOE_EUNSUPPORTED, "x_dtype=%d", x_dtype);
+  if (T == 0) return zero_counts(slot_counts, slot_offsets, num_slots, static_cast<cudaStream_t>(stream));
   if (!x || !gate_w || !workspace) return fail(B200MOE_EINVAL, "null input or workspace");
   if (H <= 0 || H % 8 != 0) return fail(B200MOE_EUNSUPPORTED, "H=%d must be a positive multiple of 8", H);
   if (ldx < H || (ldx * dtype_bytes(x_dtype)) % 16 != 0 || !aligned16(x) || !aligned16(gate_w))
@@ -225,6 +252,49 @@ int b200moe_router(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
                        status, st);
 }
 
+int b200moe_router_sigmoid_grouped(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
+                                   const float* correction_bias, int T, int H, int E, int K,
+                                   int n_group, int topk_group, int renorm, float scale,
+                                   const int32_t* log2phy, const int32_t* rep_count, int max_rep,
+                                   int num_slots, int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                                   int32_t* slot_counts, int32_t* slot_offsets, float* logits_out,
+                                   void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  int rc = check_select_args(T, E, K, num_slots, log2phy, rep_count, max_rep, topk_ids, topk_w,
+                             phys_ids, slot_counts, slot_offsets, 0, nullptr);
+  if (rc) return rc;
+  if ((rc = device_ok())) return rc;
+  if (n_group < 1 || n_group > 32 || E % n_group != 0 || E / n_group < 2 || topk_group < 1 ||
+      topk_group > n_group || K > topk_group * (E / n_group))
+    return fail(B200MOE_EUNSUPPORTED, "E=%d n_group=%d topk_group=%d K=%d: need E %% n_group == 0, "
+                "n_group <= 32, >= 2 experts per group, K <= kept experts", E, n_group, topk_group, K);
+  if (x_dtype != B200MOE_DTYPE_BF16 && x_dtype != B200MOE_DTYPE_F32)
+    return fail(B200MOE_EUNSUPPORTED, "x_dtype=%d", x_dtype);
+  if (T == 0) return zero_counts(slot_counts, slot_offsets, num_slots, static_cast<cudaStream_t>(stream));
+  if (!x || !gate_w || !workspace || !correction_bias) return fail(B200MOE_EINVAL, "null input or workspace");
+  if (H <= 0 || H % 8 != 0) return fail(B200MOE_EUNSUPPORTED, "H=%d must be a positive multiple of 8", H);
+  if (ldx < H || (ldx * dtype_bytes(x_dtype)) % 16 != 0 || !aligned16(x) || !aligned16(gate_w))
+    return fail(B200MOE_EINVAL, "x/gate_w must be 16-byte aligned with 16-byte row stride");
+  const RouterWs ws = router_ws_layout(workspace, T, E, num_slots);
+  if (workspace_bytes < ws.bytes)
+    return fail(B200MOE_EINVAL, "workspace too small: %zu < %zu", workspace_bytes, ws.bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RouterLogitsParams lp;
+  lp.x = x;
+  lp.ldx = ldx;
+  lp.w = gate_w;
+  lp.bias = nullptr;
+  lp.T = T;
+  lp.H = H;
+  lp.E1 = E;
+  lp.logits = logits_out ? logits_out : ws.logits;
+  lp.round_bf16 = 0;  // the reference computes these logits in fp32
+  launch_router_logits(lp, x_dtype, st);
+  if ((rc = check_launch("router_logits"))) return rc;
+  return select_common(lp.logits, 0, T, E, K, renorm && K > 1, scale, x_dtype == B200MOE_DTYPE_BF16,
+                       log2phy, rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, nullptr,
+                       slot_counts, slot_offsets, ws, status, st, 1, n_group, topk_group, correction_bias);
+}
+
 int b200moe_router_from_logits(const float* logits, int has_shared_gate, int T, int E, int K,
                                int renorm, float scale, int round_bf16, const int32_t* log2phy,
                                const int32_t* rep_count, int max_rep, int num_slots,
@@ -236,6 +306,7 @@ int b200moe_router_from_logits(const float* logits, int has_shared_gate, int T, 
                              phys_ids, slot_counts, slot_offsets, has_shared_gate, shared_gate);
   if (rc) return rc;
   if ((rc = device_ok())) return rc;
+  if (T == 0) return zero_counts(slot_counts, slot_offsets, num_slots, static_cast<cudaStream_t>(stream));
   if (!logits || !workspace) return fail(B200MOE_EINVAL, "null logits or workspace");
   const int E1 = E + (has_shared_gate ? 1 : 0);
   const RouterWs ws = router_ws_layout(workspace, T, E1, num_slots);
@@ -258,6 +329,7 @@ int b200moe_permute(const void* x, int64_t ldx, int x_dtype, int T, int H, int K
   if (T < 0 || K < 1 || K > 8 || H <= 0) return fail(B200MOE_EINVAL, "T=%d K=%d H=%d", T, K, H);
   const int row_bytes = H * dtype_bytes(x_dtype);
   if (row_bytes % 16 != 0) return fail(B200MOE_EUNSUPPORTED, "row bytes %d not a multiple of 16", row_bytes);
+  if (T == 0) return B200MOE_OK;
   if (!x || !phys_ids || !send || !pos_of || !workspace) return fail(B200MOE_EINVAL, "null pointer");
   if (!aligned16(x) || !aligned16(send) || (ldx * dtype_bytes(x_dtype)) % 16 != 0)
     return fail(B200MOE_EINVAL, "x/send must be 16-byte aligned with 16-byte row stride");
@@ -291,14 +363,14 @@ int b200moe_grouped_swiglu(const void* x, int64_t ldx, int64_t rows_cap,
                            void* stream) {
   int rc;
   if ((rc = device_ok())) return rc;
-  if (!x || !expert_offsets || !w_gate_up || !act) return fail(B200MOE_EINVAL, "null pointer");
   if (P < 1 || H <= 0 || I <= 0 || rows_cap < 0) return fail(B200MOE_EINVAL, "P=%d H=%d I=%d", P, H, I);
+  if (rows_cap == 0) return B200MOE_OK;  // a rank may receive no rows at all
+  if (!x || !expert_offsets || !w_gate_up || !act) return fail(B200MOE_EINVAL, "null pointer");
   if (H % 64 != 0 || I % 32 != 0)
     return fail(B200MOE_EUNSUPPORTED, "grouped_swiglu needs H %% 64 == 0 and I %% 32 == 0 (H=%d I=%d)", H, I);
   if (ldx < H || ldx % 8 != 0 || ld_act < I || ld_act % 8 != 0 || !aligned16(x) || !aligned16(act) ||
       !aligned16(w_gate_up))
     return fail(B200MOE_EINVAL, "bad leading dimension or alignment");
-  if (rows_cap == 0) return B200MOE_OK;
   GemmLaunch L;
   L.a = x;
   L.rows_cap = rows_cap;
@@ -314,6 +386,7 @@ int b200moe_grouped_swiglu(const void* x, int64_t ldx, int64_t rows_cap,
   L.p.ldo = ld_act;
   L.p.out_row_map = nullptr;
   L.p.status = status;
+  L.variant = gemm_variant_from_env();
   rc = launch_grouped_swiglu(L, static_cast<cudaStream_t>(stream));
   if (rc == -4) return fail(B200MOE_EUNSUPPORTED, "P=%d exceeds the kernel's slot limit", P);
   if (rc == -1) return fail(B200MOE_ECUDA, "cuTensorMapEncodeTiled failed (gate_up)");
@@ -327,14 +400,14 @@ int b200moe_grouped_down(const void* act, int64_t ld_act, int64_t rows_cap,
                          const int32_t* out_row_map, int* status, void* stream) {
   int rc;
   if ((rc = device_ok())) return rc;
-  if (!act || !expert_offsets || !w_down || !out) return fail(B200MOE_EINVAL, "null pointer");
   if (P < 1 || H <= 0 || I <= 0 || rows_cap < 0) return fail(B200MOE_EINVAL, "P=%d H=%d I=%d", P, H, I);
+  if (rows_cap == 0) return B200MOE_OK;
+  if (!act || !expert_offsets || !w_down || !out) return fail(B200MOE_EINVAL, "null pointer");
   if (H % 32 != 0 || I % 64 != 0)
     return fail(B200MOE_EUNSUPPORTED, "grouped_down needs H %% 32 == 0 and I %% 64 == 0 (H=%d I=%d)", H, I);
   if (ld_act < I || ld_act % 8 != 0 || ldo < H || ldo % 8 != 0 || !aligned16(act) || !aligned16(out) ||
       !aligned16(w_down))
     return fail(B200MOE_EINVAL, "bad leading dimension or alignment");
-  if (rows_cap == 0) return B200MOE_OK;
   GemmLaunch L;
   L.a = act;
   L.rows_cap = rows_cap;
@@ -350,11 +423,40 @@ int b200moe_grouped_down(const void* act, int64_t ld_act, int64_t rows_cap,
   L.p.ldo = ldo;
   L.p.out_row_map = out_row_map;
   L.p.status = status;
+  L.variant = gemm_variant_from_env();
   rc = launch_grouped_down(L, static_cast<cudaStream_t>(stream));
   if (rc == -4) return fail(B200MOE_EUNSUPPORTED, "P=%d exceeds the kernel's slot limit", P);
   if (rc == -1) return fail(B200MOE_ECUDA, "cuTensorMapEncodeTiled failed (down)");
   if (rc) return fail(B200MOE_ECUDA, "grouped_down launch: %s", cudaGetErrorString(cudaGetLastError()));
   return check_launch("grouped_down");
+}
+
+int b200moe_grouped_swiglu_f32(const float* x, int64_t ldx, int64_t rows_cap,
+                               const int32_t* expert_offsets, int P, int H, int I,
+                               const float* w_gate_up, float* act, int64_t ld_act, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (P < 1 || H <= 0 || I <= 0 || rows_cap < 0) return fail(B200MOE_EINVAL, "P=%d H=%d I=%d", P, H, I);
+  if (rows_cap == 0) return B200MOE_OK;
+  if (!x || !expert_offsets || !w_gate_up || !act) return fail(B200MOE_EINVAL, "null pointer");
+  if (ldx < H || ld_act < I) return fail(B200MOE_EINVAL, "bad leading dimension");
+  GemmF32Params p{x, ldx, rows_cap, w_gate_up, expert_offsets, P, I, H, 2 * I, I, act, ld_act, nullptr};
+  launch_grouped_gemm_f32(p, true, static_cast<cudaStream_t>(stream));
+  return check_launch("grouped_swiglu_f32");
+}
+
+int b200moe_grouped_down_f32(const float* act, int64_t ld_act, int64_t rows_cap,
+                             const int32_t* expert_offsets, int P, int H, int I, const float* w_down,
+                             float* out, int64_t ldo, const int32_t* out_row_map, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (P < 1 || H <= 0 || I <= 0 || rows_cap < 0) return fail(B200MOE_EINVAL, "P=%d H=%d I=%d", P, H, I);
+  if (rows_cap == 0) return B200MOE_OK;
+  if (!act || !expert_offsets || !w_down || !out) return fail(B200MOE_EINVAL, "null pointer");
+  if (ld_act < I || ldo < H) return fail(B200MOE_EINVAL, "bad leading dimension");
+  GemmF32Params p{act, ld_act, rows_cap, w_down, expert_offsets, P, H, I, H, 0, out, ldo, out_row_map};
+  launch_grouped_gemm_f32(p, false, static_cast<cudaStream_t>(stream));
+  return check_launch("grouped_down_f32");
 }
 
 int b200moe_combine(const void* y, int64_t ldy, int dtype, const int32_t* pos_of,
@@ -387,6 +489,37 @@ int b200moe_combine(const void* y, int64_t ldy, int dtype, const int32_t* pos_of
   p.ldo = ldo;
   launch_combine(p, static_cast<cudaStream_t>(stream));
   return check_launch("combine");
+}
+
+int b200moe_add_rmsnorm(const void* residual, const void* hidden, const void* weight, float eps,
+                        int T, int H, int dtype, int64_t ld, void* residual_out, void* normed,
+                        int64_t ld_normed, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (dtype != B200MOE_DTYPE_BF16 && dtype != B200MOE_DTYPE_F32) return fail(B200MOE_EUNSUPPORTED, "dtype=%d", dtype);
+  if (T < 0 || H <= 0) return fail(B200MOE_EINVAL, "T=%d H=%d", T, H);
+  if (T == 0) return B200MOE_OK;
+  const int eb = dtype_bytes(dtype);
+  if (!residual || !residual_out || (normed && !weight)) return fail(B200MOE_EINVAL, "null pointer");
+  if ((H * eb) % 16 || (ld * eb) % 16 || ld < H || !aligned16(residual) || !aligned16(residual_out) ||
+      (hidden && !aligned16(hidden)) || (normed && (!aligned16(normed) || !aligned16(weight) ||
+                                                    (ld_normed * eb) % 16 || ld_normed < H)))
+    return fail(B200MOE_EINVAL, "rows must be 16-byte aligned multiples of 16 bytes");
+  AddNormParams p;
+  p.residual = residual;
+  p.hidden = hidden;
+  p.weight = weight;
+  p.eps = eps;
+  p.T = T;
+  p.H = H;
+  p.dtype = dtype;
+  p.ld = ld;
+  p.residual_out = residual_out;
+  p.normed = normed;
+  p.ld_normed = ld_normed;
+  if (launch_add_rmsnorm(p, static_cast<cudaStream_t>(stream)) != 0)
+    return fail(B200MOE_EUNSUPPORTED, "add_rmsnorm supports rows up to 32 KB (H=%d)", H);
+  return check_launch("add_rmsnorm");
 }
 
 int b200moe_gather_segments(const void* src, void* dst, int64_t row_bytes,

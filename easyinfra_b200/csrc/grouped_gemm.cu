@@ -33,9 +33,13 @@ constexpr int GM_UMMA_K = 16;
 constexpr int GM_MAXP = 512;
 constexpr int GM_THREADS = 192;
 
-template <int BN, int STAGES, bool SWIGLU>
+// BMA = activation rows loaded per tile (GM_BM for prefill; fewer for decode, where an
+// expert sees only a few rows: the MMA still runs M = 128 and the accumulator rows
+// past BMA are never stored, but only BMA rows cross L2 per k-block).
+template <int BN, int STAGES, bool SWIGLU, int BMA = GM_BM>
 struct GemmShape {
-  static constexpr int A_BYTES = GM_BM * GM_BK * 2;
+  static constexpr int A_BYTES = GM_BM * GM_BK * 2;     // smem per A stage (MMA reads 128 rows)
+  static constexpr int A_LOAD_BYTES = BMA * GM_BK * 2;  // bytes TMA writes per A stage
   static constexpr int B_BYTES = BN * GM_BK * 2;
   static constexpr int OUT_COLS = SWIGLU ? BN / 2 : BN;
   static constexpr int TMEM_COLS = 2 * BN;  // two fp32 accumulators
@@ -43,8 +47,10 @@ struct GemmShape {
   static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + CTRL_BYTES;
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
   static_assert(BN % 32 == 0 && BN <= 256, "BN");
+  static_assert(BMA % 32 == 0 && BMA <= GM_BM, "BMA");
 };
 
+template <int BMA>
 __device__ __forceinline__ void decode_tile(const int* prefix, const int32_t* off, int P, int tile,
                                             int& e, int& m, int& n) {
   int lo = 0, hi = P - 1;
@@ -55,18 +61,18 @@ __device__ __forceinline__ void decode_tile(const int* prefix, const int32_t* of
   e = lo;
   const int local = tile - prefix[e];
   const int rows = off[e + 1] - off[e];
-  const int mt = (rows + GM_BM - 1) / GM_BM;
+  const int mt = (rows + BMA - 1) / BMA;
   n = local / mt;
   m = local - n * mt;
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
-template <int BN, int STAGES, bool SWIGLU>
+template <int BN, int STAGES, bool SWIGLU, int BMA>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                         const __grid_constant__ CUtensorMap map_b, GemmParams p) {
-  using S = GemmShape<BN, STAGES, SWIGLU>;
+  using S = GemmShape<BN, STAGES, SWIGLU, BMA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       int c = 0;
       if (e < p.P) {
         const int rows = off[e + 1] - off[e];
-        c = ((rows + GM_BM - 1) / GM_BM) * nt;
+        c = ((rows + BMA - 1) / BMA) * nt;
       }
       int incl = c;
 #pragma unroll
@@ -142,12 +148,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
         int e, m, n;
-        decode_tile(prefix, off, p.P, tile, e, m, n);
-        const int row_a = off[e] + m * GM_BM;
+        decode_tile<BMA>(prefix, off, p.P, tile, e, m, n);
+        const int row_a = off[e] + m * BMA;
         const int row_b = e * p.w_rows + n * S::OUT_COLS;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], S::A_BYTES + S::B_BYTES);
+          mbar_arrive_expect_tx(&full[stage], S::A_LOAD_BYTES + S::B_BYTES);
           tma_load_2d(sa + stage * S::A_BYTES, &map_a, &full[stage], kb * GM_BK, row_a);
           if (SWIGLU) {
             uint8_t* dst = sb + stage * S::B_BYTES;
@@ -198,15 +204,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     // -------------------------------------------------- epilogue (warps 2..5)
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
     const int row_in_tile = quarter * 32 + lane;
+    const bool warp_has_rows = quarter * 32 < BMA;  // lanes past BMA hold no loaded rows
     int acc = 0;
     uint32_t acc_phase = 0;
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       int e, m, n;
-      decode_tile(prefix, off, p.P, tile, e, m, n);
+      decode_tile<BMA>(prefix, off, p.P, tile, e, m, n);
       const int rows = off[e + 1] - off[e];
-      const int r = m * GM_BM + row_in_tile;
-      const bool valid = r < rows;
+      const int r = m * BMA + row_in_tile;
+      const bool valid = warp_has_rows && r < rows;
       const int64_t grow = static_cast<int64_t>(off[e]) + r;
       int64_t orow = grow;
       if (valid && p.out_row_map != nullptr) orow = p.out_row_map[grow];
@@ -218,7 +225,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       __nv_bfloat16* orow_ptr = out + orow * p.ldo;
-      if (SWIGLU) {
+      if (!warp_has_rows) {
+        // nothing of this tile lives in this warp's TMEM lanes
+      } else if (SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           uint32_t g[32], u[32];
@@ -305,8 +314,8 @@ static EncodeTiledFn get_encode_fn() {
 
 // 2D bf16 K-major map: rows x cols (cols contiguous, row stride ld elements), box
 // box_rows x 64 with the 128-byte swizzle.
-static int make_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
-                       int box_rows) {
+int make_tma_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                    int box_rows) {
   EncodeTiledFn fn = get_encode_fn();
   if (fn == nullptr) return -1;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
@@ -319,13 +328,13 @@ static int make_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-template <int BN, int STAGES, bool SWIGLU>
+template <int BN, int STAGES, bool SWIGLU, int BMA>
 static int run_gemm(const GemmLaunch& L, cudaStream_t stream) {
-  using S = GemmShape<BN, STAGES, SWIGLU>;
+  using S = GemmShape<BN, STAGES, SWIGLU, BMA>;
   static_assert(S::SMEM_BYTES <= 232448, "shared memory");
   CUtensorMap ma, mb;
-  if (make_map_2d(&ma, L.a, L.rows_cap, L.p.K, L.lda, GM_BM) != 0) return -1;
-  if (make_map_2d(&mb, L.w, static_cast<int64_t>(L.p.P) * L.p.w_rows, L.p.K, L.p.K,
+  if (make_tma_map_2d(&ma, L.a, L.rows_cap, L.p.K, L.lda, BMA) != 0) return -1;
+  if (make_tma_map_2d(&mb, L.w, static_cast<int64_t>(L.p.P) * L.p.w_rows, L.p.K, L.p.K,
                   SWIGLU ? BN / 2 : BN) != 0)
     return -1;
   // Request at least half the SM's shared memory so two CTAs never share one SM
@@ -336,27 +345,39 @@ static int run_gemm(const GemmLaunch& L, cudaStream_t stream) {
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set_mask & bit)) {
-    if (cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, SWIGLU>,
+    if (cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, SWIGLU, BMA>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return -3;
     attr_set_mask |= bit;
   }
   const int nt = (L.p.N + S::OUT_COLS - 1) / S::OUT_COLS;
-  const int64_t bound = ((L.rows_cap + GM_BM - 1) / GM_BM + L.p.P) * static_cast<int64_t>(nt);
+  const int64_t bound = ((L.rows_cap + BMA - 1) / BMA + L.p.P) * static_cast<int64_t>(nt);
   const int grid = static_cast<int>(bound < num_sms() ? bound : num_sms());
   if (grid <= 0) return 0;
-  grouped_gemm_kernel<BN, STAGES, SWIGLU><<<grid, GM_THREADS, smem, stream>>>(ma, mb, L.p);
+  grouped_gemm_kernel<BN, STAGES, SWIGLU, BMA><<<grid, GM_THREADS, smem, stream>>>(ma, mb, L.p);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// Decode regime (few rows per expert on average): the GEMM streams weights and is
+// HBM-bound; the weight-major kernel (grouped_gemm_wm.cu) keeps the most weight
+// bytes in flight.  The token-major kernel with 32-row activation tiles remains
+// available (GemmVariant::kTokenMajorSmallM) for comparison.
+static bool decode_regime(const GemmLaunch& L) { return L.rows_cap <= 48 * static_cast<int64_t>(L.p.P); }
+
 int launch_grouped_swiglu(const GemmLaunch& L, cudaStream_t stream) {
   if (L.p.P > GM_MAXP) return -4;
-  return run_gemm<256, 4, true>(L, stream);
+  const int v = L.variant;
+  if (v == kGemmWeightMajor || (v == kGemmAuto && decode_regime(L))) return launch_grouped_wm(L, true, stream);
+  if (v == kGemmTokenMajorSmallM) return run_gemm<64, 9, true, 32>(L, stream);
+  return run_gemm<256, 4, true, GM_BM>(L, stream);
 }
 
 int launch_grouped_down(const GemmLaunch& L, cudaStream_t stream) {
   if (L.p.P > GM_MAXP) return -4;
-  return run_gemm<256, 4, false>(L, stream);
+  const int v = L.variant;
+  if (v == kGemmWeightMajor || (v == kGemmAuto && decode_regime(L))) return launch_grouped_wm(L, false, stream);
+  if (v == kGemmTokenMajorSmallM) return run_gemm<64, 9, false, 32>(L, stream);
+  return run_gemm<256, 4, false, GM_BM>(L, stream);
 }
 
 }  // namespace b200moe

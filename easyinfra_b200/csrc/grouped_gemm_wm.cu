@@ -1,0 +1,289 @@
+// Kernel family (3), decode regime: "weight-major" grouped expert GEMMs.
+//
+// Same contract as grouped_gemm.cu (expert-major rows, stacked weights, fused
+// SwiGLU, optional output row map) with the operands swapped for few tokens per
+// expert: the streamed weights are the MMA's A operand (M = 128 weight rows) and
+// the expert's token rows are B (N = NTOK), so every byte of shared memory in the
+// pipeline carries weights and ~10 stages of 16 KB stay in flight per SM — the
+// regime is HBM-bound and bytes in flight are what sustain bandwidth.
+//   * tile = (expert, feature block, token block): 128 output features (SwiGLU:
+//     64 gate + 64 up rows of the same 64 features) x NTOK tokens;
+//   * accumulator D[features, tokens] in TMEM (lane = feature), double-buffered;
+//   * epilogue: a warp holds 32 consecutive features of every token, so each token's
+//     store is one coalesced 64-byte run; for SwiGLU the up half (lanes 64..127) is
+//     handed to the gate warps through shared memory;
+//   * per-CTA TMA loads only (no clusters), bounded mbarrier waits.
+#include "kernels.cuh"
+
+namespace b200moe {
+
+constexpr int WM_M = 128;    // weight rows per tile (UMMA M)
+constexpr int WM_BK = 64;
+constexpr int WM_MAXP = 512;
+constexpr int WM_THREADS = 192;
+
+template <int NTOK, int STAGES, bool SWIGLU>
+struct WmShape {
+  static constexpr int A_BYTES = WM_M * WM_BK * 2;      // 16 KB of weights per stage
+  static constexpr int B_BYTES = NTOK * WM_BK * 2;      // token rows per stage
+  static constexpr int FEAT = SWIGLU ? WM_M / 2 : WM_M; // output features per tile
+  static constexpr int TMEM_COLS = (2 * NTOK < 32) ? 32 : 2 * NTOK;
+  static constexpr int UP_LD = NTOK + 1;                // padded row of the up exchange buffer
+  static constexpr int XCHG_BYTES = SWIGLU ? 64 * UP_LD * 4 : 0;
+  static constexpr int CTRL_BYTES = 512 + 2 * (WM_MAXP + 1) * 4;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + XCHG_BYTES + CTRL_BYTES;
+  static_assert(NTOK % 16 == 0 && NTOK >= 16 && NTOK <= 256, "UMMA N for M = 128");
+  static_assert(NTOK <= 32, "epilogue loads NTOK columns with one 32x32b.x32 load");
+};
+
+__device__ __forceinline__ void wm_decode_tile(const int* prefix, const int32_t* off, int P, int ntok,
+                                               int tile, int& e, int& m, int& n) {
+  int lo = 0, hi = P - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= tile) lo = mid; else hi = mid - 1;
+  }
+  e = lo;
+  const int local = tile - prefix[e];
+  const int rows = off[e + 1] - off[e];
+  const int mt = (rows + ntok - 1) / ntok;
+  n = local / mt;
+  m = local - n * mt;
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int NTOK, int STAGES, bool SWIGLU>
+__global__ void __launch_bounds__(WM_THREADS, 1)
+    grouped_gemm_wm_kernel(const __grid_constant__ CUtensorMap map_w,
+                           const __grid_constant__ CUtensorMap map_x, GemmParams p) {
+  using S = WmShape<NTOK, STAGES, SWIGLU>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sa = smem;                                   // weights
+  uint8_t* sb = smem + STAGES * S::A_BYTES;             // tokens
+  float* up_buf = reinterpret_cast<float*>(sb + STAGES * S::B_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + STAGES * S::B_BYTES + S::XCHG_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* tile_ok = reinterpret_cast<volatile int*>(tmem_holder + 2);  // epilogue handshake
+  int* prefix = reinterpret_cast<int*>(tmem_holder + 4);
+  int32_t* off = prefix + (WM_MAXP + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = (p.N + S::FEAT - 1) / S::FEAT;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_w);
+    tma_prefetch_desc(&map_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 2) {
+    for (int base = 0; base <= p.P; base += 32) {
+      const int e = base + lane;
+      if (e <= p.P) off[e] = p.expert_offsets[e];
+    }
+    __syncwarp();
+    int run = 0;
+    for (int base = 0; base < p.P; base += 32) {
+      const int e = base + lane;
+      int c = 0;
+      if (e < p.P) c = ((off[e + 1] - off[e] + NTOK - 1) / NTOK) * nt;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (e < p.P) prefix[e] = run + incl - c;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) prefix[p.P] = run;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int total_tiles = prefix[p.P];
+  const int num_kb = (p.K + WM_BK - 1) / WM_BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      const uint64_t stream_once = l2_policy_evict_first();  // weights are read once
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+        int e, m, n;
+        wm_decode_tile(prefix, off, p.P, NTOK, tile, e, m, n);
+        const int row_w = e * p.w_rows + n * S::FEAT;
+        const int row_x = off[e] + m * NTOK;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], S::A_BYTES + S::B_BYTES);
+          uint8_t* dst = sa + stage * S::A_BYTES;
+          if (SWIGLU) {
+            tma_load_2d_hint(dst, &map_w, &full[stage], kb * WM_BK, row_w, stream_once);
+            tma_load_2d_hint(dst + 64 * 128, &map_w, &full[stage], kb * WM_BK, row_w + p.up_row, stream_once);
+          } else {
+            tma_load_2d_hint(dst, &map_w, &full[stage], kb * WM_BK, row_w, stream_once);
+          }
+          tma_load_2d(sb + stage * S::B_BYTES, &map_x, &full[stage], kb * WM_BK, row_x);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = make_idesc_bf16_f32(WM_M, NTOK);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * NTOK);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_kmajor_desc(smem_u32(sa + stage * S::A_BYTES));
+          const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(sb + stage * S::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < WM_BK / 16; ++k)
+            umma_bf16(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------------------------- epilogue (warps 2..5)
+    const int quarter = warp & 3;          // TMEM lanes = tile rows (features) 32q..32q+31
+    const int feat = quarter * 32 + lane;  // row of the weight tile this thread holds
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      int e, m, n;
+      wm_decode_tile(prefix, off, p.P, NTOK, tile, e, m, n);
+      const int rows = off[e + 1] - off[e];
+      const int tok0 = m * NTOK;
+      const int ntok = min(NTOK, rows - tok0);
+      // One thread waits (bounded); the outcome reaches all four epilogue warps through
+      // shared memory and the named barrier, so they all continue or all stop together
+      // and no warp can be left waiting at a later barrier.
+      if (warp == 2 && lane == 0) *tile_ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status) ? 1 : 0;
+      epi_bar();
+      if (*tile_ok == 0) break;
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * NTOK),
+                         v);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);  // accumulator copied to registers
+      if (SWIGLU) {
+        if (quarter >= 2) {
+          float* u = up_buf + (feat - 64) * S::UP_LD;
+#pragma unroll
+          for (int j = 0; j < NTOK; ++j) u[j] = __uint_as_float(v[j]);
+        }
+        epi_bar();
+        if (quarter < 2) {
+          const int col = n * S::FEAT + feat;
+          const float* u = up_buf + feat * S::UP_LD;
+          if (col < p.N) {
+            for (int j = 0; j < ntok; ++j) {
+              const int64_t grow = static_cast<int64_t>(off[e]) + tok0 + j;
+              const float g = __uint_as_float(v[j]);
+              out[grow * p.ldo + col] = __float2bfloat16_rn(g / (1.f + expf(-g)) * u[j]);
+            }
+          }
+        }
+      } else {
+        const int col = n * S::FEAT + feat;
+        if (col < p.N) {
+          for (int j = 0; j < ntok; ++j) {
+            int64_t grow = static_cast<int64_t>(off[e]) + tok0 + j;
+            if (p.out_row_map != nullptr) grow = p.out_row_map[grow];
+            out[grow * p.ldo + col] = __float2bfloat16_rn(__uint_as_float(v[j]));
+          }
+        }
+      }
+      epi_bar();  // tile_ok and up_buf are rewritten for the next tile
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+template <int NTOK, int STAGES, bool SWIGLU>
+static int run_wm(const GemmLaunch& L, cudaStream_t stream) {
+  using S = WmShape<NTOK, STAGES, SWIGLU>;
+  static_assert(S::SMEM_BYTES <= 232448, "shared memory");
+  CUtensorMap mw, mx;
+  if (make_tma_map_2d(&mw, L.w, static_cast<int64_t>(L.p.P) * L.p.w_rows, L.p.K, L.p.K,
+                      SWIGLU ? WM_M / 2 : WM_M) != 0)
+    return -1;
+  if (make_tma_map_2d(&mx, L.a, L.rows_cap, L.p.K, L.lda, NTOK) != 0) return -1;
+  const int smem = S::SMEM_BYTES > 120 * 1024 ? S::SMEM_BYTES : 120 * 1024;
+  static uint64_t attr_set_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set_mask & bit)) {
+    if (cudaFuncSetAttribute(grouped_gemm_wm_kernel<NTOK, STAGES, SWIGLU>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return -3;
+    attr_set_mask |= bit;
+  }
+  const int nt = (L.p.N + S::FEAT - 1) / S::FEAT;
+  const int64_t bound = ((L.rows_cap + NTOK - 1) / NTOK + L.p.P) * static_cast<int64_t>(nt);
+  const int grid = static_cast<int>(bound < num_sms() ? bound : num_sms());
+  if (grid <= 0) return 0;
+  grouped_gemm_wm_kernel<NTOK, STAGES, SWIGLU><<<grid, WM_THREADS, smem, stream>>>(mw, mx, L.p);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int launch_grouped_wm(const GemmLaunch& L, bool swiglu, cudaStream_t stream) {
+  if (L.p.P > WM_MAXP) return -4;
+  return swiglu ? run_wm<32, 10, true>(L, stream) : run_wm<32, 10, false>(L, stream);
+}
+
+}  // namespace b200moe

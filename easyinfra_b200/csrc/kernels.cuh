@@ -14,6 +14,7 @@ struct RouterLogitsParams {
   const float* bias;   // [E1] or null
   int T, H, E1;
   float* logits;       // [T, E1]
+  int round_bf16 = 1;  // round bf16 logits like F.linear's bf16 output (0: keep fp32)
 };
 
 struct RouterSelectParams {
@@ -38,6 +39,11 @@ struct RouterSelectParams {
   int32_t* slot_offsets; // [num_slots + 1]
   uint32_t* ticket;      // zero before the first call; the last CTA resets it
   int* status;
+  // scoring 0: softmax top-k (Qwen3MoeSparseMoeBlock._routing);
+  // scoring 1: sigmoid + correction bias + group-limited top-k (DeepseekV3MoEGate)
+  int scoring = 0;
+  int n_group = 1, topk_group = 1;
+  const float* correction_bias = nullptr;  // [E]
 };
 
 // ---- permute / combine (permute.cu)
@@ -69,6 +75,19 @@ struct CombineParams {
   int64_t ldo;
 };
 
+// ---- residual add + RMSNorm (norm.cu)
+struct AddNormParams {
+  const void* residual;   // [T, H] (row stride ld)
+  const void* hidden;     // [T, H] or null (no add)
+  const void* weight;     // [H] norm weight (dtype of the activations)
+  float eps;
+  int T, H, dtype;
+  int64_t ld;             // elements, shared by residual / hidden / residual_out
+  void* residual_out;     // [T, H] (may alias residual)
+  void* normed;           // [T, H] or null (add only)
+  int64_t ld_normed;
+};
+
 // ---- grouped GEMM (grouped_gemm.cu)
 struct GemmParams {
   const int32_t* expert_offsets;  // [P+1]: rows of expert p are [off[p], off[p+1])
@@ -83,18 +102,47 @@ struct GemmParams {
   int* status;
 };
 
+// Grouped-GEMM kernel choice: automatic (by rows per slot), or forced for tests.
+enum GemmVariant : int {
+  kGemmAuto = 0,
+  kGemmTokenMajor = 1,        // M = 128 token rows x N = 256 weight rows (prefill)
+  kGemmTokenMajorSmallM = 2,  // 32 token rows per tile, N = 64
+  kGemmWeightMajor = 3,       // M = 128 weight rows x N = 32 tokens (decode)
+};
+
 struct GemmLaunch {
   const void* a;        // [rows_cap, K] bf16 activations, row stride lda
   int64_t rows_cap;
   int64_t lda;
   const void* w;        // [P * w_rows, K] bf16 weights (row stride K)
   GemmParams p;
+  int variant = kGemmAuto;
+};
+
+// 2D bf16 K-major TMA map (rows x cols, row stride ld elements), box box_rows x 64,
+// 128-byte swizzle.  Returns 0 on success.
+int make_tma_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                    int box_rows);
+int launch_grouped_wm(const GemmLaunch& L, bool swiglu, cudaStream_t stream);
+
+struct GemmF32Params {
+  const float* a;          // [rows, K]
+  int64_t lda;
+  int64_t rows_cap;
+  const float* w;          // [P, w_rows, K]
+  const int32_t* offsets;  // [P+1]
+  int P, N, K, w_rows, up_row;
+  float* out;
+  int64_t ldo;
+  const int32_t* out_row_map;
 };
 
 int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t stream);
+int launch_grouped_gemm_f32(const GemmF32Params& p, bool swiglu, cudaStream_t stream);
 int launch_router_select(const RouterSelectParams& p, cudaStream_t stream);
 int launch_permute(const PermuteParams& p, cudaStream_t stream);
 int launch_combine(const CombineParams& p, cudaStream_t stream);
+int launch_add_rmsnorm(const AddNormParams& p, cudaStream_t stream);
 // Return 0, -1 (tensor map encode failed), -3 (launch failed), -4 (P too large).
 int launch_grouped_swiglu(const GemmLaunch& L, cudaStream_t stream);
 int launch_grouped_down(const GemmLaunch& L, cudaStream_t stream);

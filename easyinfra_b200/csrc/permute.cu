@@ -117,37 +117,44 @@ __device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
+// One warp per (token, 256-column chunk): all K expert rows of the chunk are loaded
+// before any arithmetic, so a token's gathers are in flight together.
 template <typename E>
 __global__ void __launch_bounds__(256) combine_rows(CombineParams p) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= p.T) return;
-  const int t = warp;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int chunks = (p.H + 255) / 256;
+  if (gw >= static_cast<int64_t>(p.T) * chunks) return;
+  const int t = static_cast<int>(gw / chunks);
+  const int c = static_cast<int>(gw - static_cast<int64_t>(t) * chunks) * 256 + lane * 8;
+  if (c >= p.H) return;
   const E* y = static_cast<const E*>(p.y);
-  int rows[8];
+  float v[8][8];
   float wts[8];
-  for (int k = 0; k < p.K; ++k) {
-    rows[k] = p.pos_of[static_cast<int64_t>(t) * p.K + k];
-    wts[k] = p.topk_w[static_cast<int64_t>(t) * p.K + k];
-  }
-  const float g = p.shared_gate ? p.shared_gate[t] : 1.f;
-  const E* sh = p.shared ? static_cast<const E*>(p.shared) + static_cast<int64_t>(t) * p.lds : nullptr;
-  E* out = static_cast<E*>(p.out) + static_cast<int64_t>(t) * p.ldo;
-  for (int c = lane * 8; c < p.H; c += 32 * 8) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int k = 0; k < p.K; ++k) {
-      float v[8];
-      load8<E>(y + static_cast<int64_t>(rows[k]) * p.ldy + c, v);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = fmaf(wts[k], v[i], acc[i]);
+  for (int k = 0; k < 8; ++k) {
+    if (k < p.K) {
+      const int row = p.pos_of[static_cast<int64_t>(t) * p.K + k];
+      wts[k] = p.topk_w[static_cast<int64_t>(t) * p.K + k];
+      load8<E>(y + static_cast<int64_t>(row) * p.ldy + c, v[k]);
     }
-    if (sh) {
-      float v[8];
-      load8<E>(sh + c, v);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = fmaf(g, v[i], acc[i]);
-    }
-    store8<E>(out + c, acc);
   }
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    if (k < p.K) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(wts[k], v[k][i], acc[i]);
+    }
+  }
+  if (p.shared) {
+    const float g = p.shared_gate ? p.shared_gate[t] : 1.f;
+    float s[8];
+    load8<E>(static_cast<const E*>(p.shared) + static_cast<int64_t>(t) * p.lds + c, s);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = fmaf(g, s[i], acc[i]);
+  }
+  store8<E>(static_cast<E*>(p.out) + static_cast<int64_t>(t) * p.ldo + c, acc);
 }
 
 int launch_permute(const PermuteParams& p, cudaStream_t stream) {
@@ -159,7 +166,8 @@ int launch_permute(const PermuteParams& p, cudaStream_t stream) {
 
 int launch_combine(const CombineParams& p, cudaStream_t stream) {
   if (p.T == 0) return 0;
-  const int grid = (p.T * 32 + 255) / 256;
+  const int64_t warps = static_cast<int64_t>(p.T) * ((p.H + 255) / 256);
+  const int grid = static_cast<int>((warps * 32 + 255) / 256);
   if (p.dtype == kDtypeBF16)
     combine_rows<__nv_bfloat16><<<grid, 256, 0, stream>>>(p);
   else

@@ -102,10 +102,63 @@ __global__ void __launch_bounds__(128) router_logits_bf16(RouterLogitsParams p, 
         if (row < p.T && col < ncols) {
           float v = acc[j][q];
           if (p.bias) v += p.bias[col0 + col];
-          p.logits[static_cast<int64_t>(row) * p.E1 + col0 + col] = bf16_round(v);
+          p.logits[static_cast<int64_t>(row) * p.E1 + col0 + col] = p.round_bf16 ? bf16_round(v) : v;
         }
       }
     }
+  }
+}
+
+// ------------------------------------------------------------------ logits (small T)
+// Decode-sized batches: one CTA per (router column, group of RG tokens); its 256
+// threads stride over the hidden dimension with 16-byte loads (the weight row is
+// read once per group), keep RG partial dot products in registers, and reduce them
+// through shared memory in a fixed order (deterministic, no atomics).
+constexpr int RG = 8;
+
+template <typename E>
+__global__ void __launch_bounds__(256) router_logits_gemv(RouterLogitsParams p) {
+  __shared__ float red[8][RG];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.y, t0 = blockIdx.x * RG;
+  const int nt = min(RG, p.T - t0);
+  constexpr int V = 16 / sizeof(E);
+  const E* w = static_cast<const E*>(p.w) + static_cast<int64_t>(e) * p.H;
+  const E* x = static_cast<const E*>(p.x) + static_cast<int64_t>(t0) * p.ldx;
+  float acc[RG];
+#pragma unroll
+  for (int i = 0; i < RG; ++i) acc[i] = 0.f;
+  for (int c = threadIdx.x * V; c < p.H; c += 256 * V) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + c));
+    uint4 xv[RG];
+#pragma unroll
+    for (int i = 0; i < RG; ++i)
+      xv[i] = (i < nt) ? __ldg(reinterpret_cast<const uint4*>(x + i * p.ldx + c)) : make_uint4(0, 0, 0, 0);
+    const E* we = reinterpret_cast<const E*>(&wv);
+#pragma unroll
+    for (int i = 0; i < RG; ++i) {
+      const E* xe = reinterpret_cast<const E*>(&xv[i]);
+#pragma unroll
+      for (int j = 0; j < V; ++j) acc[i] = fmaf(static_cast<float>(xe[j]), static_cast<float>(we[j]), acc[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RG; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < RG; ++i) red[warp][i] = acc[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < nt) {
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v += red[q][threadIdx.x];
+    if (p.bias) v += p.bias[e];
+    if (sizeof(E) == 2 && p.round_bf16) v = bf16_round(v);
+    p.logits[static_cast<int64_t>(t0 + threadIdx.x) * p.E1 + e] = v;
   }
 }
 
@@ -148,8 +201,9 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
 }
 
 __global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
-  extern __shared__ int32_t hist[];  // [num_slots]
+  extern __shared__ int32_t hist[];  // [num_slots], then (scoring 1) 8 warps x 256 floats
   __shared__ int s_last;
+  float* cbuf = reinterpret_cast<float*>(hist + p.num_slots) + (threadIdx.x >> 5) * 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) hist[s] = 0;
   __syncthreads();
@@ -158,60 +212,117 @@ __global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
   const int t_end = min(p.T, t_begin + p.tb);
   for (int t = t_begin + warp; t < t_end; t += blockDim.x >> 5) {
     const float* lg = p.logits + static_cast<int64_t>(t) * p.E1;
-    float v[RS_MAXJ];
-    float m = -INFINITY;
+    float v[RS_MAXJ];     // selection key per owned expert
+    float sc[RS_MAXJ];    // value reported as the routing weight (before renorm)
+    if (p.scoring == 0) {
+      // softmax over the experts (fp32), select on the probabilities
+      float m = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < RS_MAXJ; ++j) {
-      const int e = lane + 32 * j;
-      v[j] = (e < p.E) ? lg[e] : -INFINITY;
-      m = fmaxf(m, v[j]);
+      for (int j = 0; j < RS_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        v[j] = (e < p.E) ? lg[e] : -INFINITY;
+        m = fmaxf(m, v[j]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < RS_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        v[j] = (e < p.E) ? expf(v[j] - m) : 0.f;
+        s += v[j];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+#pragma unroll
+      for (int j = 0; j < RS_MAXJ; ++j) {
+        v[j] = (lane + 32 * j < p.E) ? v[j] / s : -1.f;
+        sc[j] = v[j];
+      }
+    } else {
+      // sigmoid scores; choice = score + correction bias; keep the topk_group groups
+      // with the largest sum of their two best choices; others' choices become 0.0
+      const int gs = p.E / p.n_group;
+#pragma unroll
+      for (int j = 0; j < RS_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        if (e < p.E) {
+          sc[j] = 1.f / (1.f + expf(-lg[e]));
+          v[j] = sc[j] + p.correction_bias[e];
+          cbuf[e] = v[j];
+        } else {
+          sc[j] = 0.f;
+          v[j] = -INFINITY;
+        }
+      }
+      __syncwarp();
+      float gsum = -INFINITY;
+      if (lane < p.n_group) {
+        float b1 = -INFINITY, b2 = -INFINITY;
+        for (int q = 0; q < gs; ++q) {
+          const float c = cbuf[lane * gs + q];
+          if (c > b1) { b2 = b1; b1 = c; } else if (c > b2) { b2 = c; }
+        }
+        gsum = b1 + b2;
+      }
+      uint32_t keep = 0;
+      for (int r = 0; r < p.topk_group; ++r) {
+        float bv = ((keep >> lane) & 1u) ? -INFINITY : gsum;
+        int bi = (lane < p.n_group && !((keep >> lane) & 1u)) ? lane : 0x7fffffff;
+        if (bi == 0x7fffffff) bv = -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if (bi < 32) keep |= 1u << bi;
+      }
+#pragma unroll
+      for (int j = 0; j < RS_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        if (e < p.E && !((keep >> (e / gs)) & 1u)) v[j] = 0.f;
+      }
+      __syncwarp();
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < RS_MAXJ; ++j) {
-      const int e = lane + 32 * j;
-      v[j] = (e < p.E) ? expf(v[j] - m) : 0.f;
-      s += v[j];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-#pragma unroll
-    for (int j = 0; j < RS_MAXJ; ++j) v[j] = (lane + 32 * j < p.E) ? v[j] / s : -1.f;
 
-    // top-k: K rounds of a warp arg-max on (prob desc, expert asc).
+    // top-k: K rounds of a warp arg-max on (key desc, expert asc); the winner's
+    // reported value (probability, or sigmoid score) travels with it.
     float selp[8];
     int sele[8];
     uint32_t taken = 0;
     for (int k = 0; k < p.K; ++k) {
-      float bv = -2.f;
+      float bv = -INFINITY, bs = 0.f;
       int bi = 0x7fffffff;
 #pragma unroll
       for (int j = 0; j < RS_MAXJ; ++j) {
         const int e = lane + 32 * j;
         if (e < p.E && !((taken >> j) & 1u) && better(v[j], e, bv, bi)) {
           bv = v[j];
+          bs = sc[j];
           bi = e;
         }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const float os = __shfl_xor_sync(0xffffffffu, bs, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (better(ov, oi, bv, bi)) {
           bv = ov;
+          bs = os;
           bi = oi;
         }
       }
       if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-      selp[k] = bv;
+      selp[k] = bs;
       sele[k] = bi;
     }
     float denom = 1.f;
     if (p.renorm) {
       denom = 0.f;
       for (int k = 0; k < p.K; ++k) denom += selp[k];
+      if (p.scoring == 1) denom += 1e-20f;
     }
     if (lane < p.K) {
       float wk = 0.f;
@@ -257,20 +368,34 @@ __global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
   // ---- last CTA: slot totals, slot offsets, absolute per-(slot, block) offsets.
   __threadfence();
   const int nb = p.nblocks;
-  const int per_lane = (nb + 31) / 32;
-  for (int s = warp; s < p.num_slots; s += blockDim.x >> 5) {
-    const int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
-    int part = 0;
-    for (int i = 0; i < per_lane; ++i) {
-      const int b = lane * per_lane + i;
-      if (b < nb) part += __ldcg(col + b);
-    }
+  constexpr int kSmallNb = 16;
+  if (nb <= kSmallNb) {
+    // few blocks (decode batches): one thread per slot, one round trip of loads
+    for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) {
+      const int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
+      int tot = 0;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (lane == 0) hist[s] = part;
+      for (int b = 0; b < kSmallNb; ++b)
+        if (b < nb) tot += __ldcg(col + b);
+      hist[s] = tot;
+    }
+  } else {
+    const int per_lane = (nb + 31) / 32;
+    for (int s = warp; s < p.num_slots; s += blockDim.x >> 5) {
+      const int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
+      int part = 0;
+      for (int i = 0; i < per_lane; ++i) {
+        const int b = lane * per_lane + i;
+        if (b < nb) part += __ldcg(col + b);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (lane == 0) hist[s] = part;
+    }
   }
   __syncthreads();
   if (warp == 0) {
+    // exclusive scan of the slot totals; hist[] becomes the slot offsets
     int run = 0;
     for (int base = 0; base < p.num_slots; base += 32) {
       const int s = base + lane;
@@ -284,32 +409,50 @@ __global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
       if (s < p.num_slots) {
         p.slot_counts[s] = c;
         p.slot_offsets[s] = run + incl - c;
+        hist[s] = run + incl - c;
       }
       run += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) p.slot_offsets[p.num_slots] = run;
   }
   __syncthreads();
-  for (int s = warp; s < p.num_slots; s += blockDim.x >> 5) {
-    int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
-    int part = 0;
-    for (int i = 0; i < per_lane; ++i) {
-      const int b = lane * per_lane + i;
-      if (b < nb) part += __ldcg(col + b);
-    }
-    int incl = part;
+  if (nb <= kSmallNb) {
+    for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) {
+      int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
+      int c[kSmallNb];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += n;
+      for (int b = 0; b < kSmallNb; ++b) c[b] = (b < nb) ? __ldcg(col + b) : 0;
+      int run = hist[s];
+#pragma unroll
+      for (int b = 0; b < kSmallNb; ++b)
+        if (b < nb) {
+          col[b] = run;
+          run += c[b];
+        }
     }
-    int run = __ldcg(p.slot_offsets + s) + incl - part;
-    for (int i = 0; i < per_lane; ++i) {
-      const int b = lane * per_lane + i;
-      if (b < nb) {
-        const int c = __ldcg(col + b);
-        col[b] = run;
-        run += c;
+  } else {
+    const int per_lane = (nb + 31) / 32;
+    for (int s = warp; s < p.num_slots; s += blockDim.x >> 5) {
+      int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
+      int part = 0;
+      for (int i = 0; i < per_lane; ++i) {
+        const int b = lane * per_lane + i;
+        if (b < nb) part += __ldcg(col + b);
+      }
+      int incl = part;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      int run = hist[s] + incl - part;
+      for (int i = 0; i < per_lane; ++i) {
+        const int b = lane * per_lane + i;
+        if (b < nb) {
+          const int c = __ldcg(col + b);
+          col[b] = run;
+          run += c;
+        }
       }
     }
   }
@@ -319,6 +462,14 @@ __global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
 // ------------------------------------------------------------------ host launchers
 int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t stream) {
   if (p.T == 0) return 0;
+  if (p.T <= 256) {
+    const dim3 grid((p.T + RG - 1) / RG, p.E1);
+    if (x_dtype == kDtypeBF16)
+      router_logits_gemv<__nv_bfloat16><<<grid, 256, 0, stream>>>(p);
+    else
+      router_logits_gemv<float><<<grid, 256, 0, stream>>>(p);
+    return 0;
+  }
   if (x_dtype == kDtypeBF16) {
     const int tok_blocks = (p.T + RL_TOK - 1) / RL_TOK;
     // Enough CTAs to cover the SMs: narrow column groups when the token count is small.
@@ -336,7 +487,8 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
 
 int launch_router_select(const RouterSelectParams& p, cudaStream_t stream) {
   if (p.T == 0) return 0;
-  const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t);
+  const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t) +
+                      (p.scoring == 1 ? 8 * 256 * sizeof(float) : 0);
   router_select<<<p.nblocks, 256, smem, stream>>>(p);
   return 0;
 }

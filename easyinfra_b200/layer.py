@@ -66,6 +66,9 @@ class LayerParams:
     gate_bias: Optional[torch.Tensor] = None     # [E(+1)] fp32
     shared_gate_up: Optional[torch.Tensor] = None  # [2Is, H]
     shared_down: Optional[torch.Tensor] = None     # [H, Is]
+    norm_weight: Optional[torch.Tensor] = None     # [H] post_attention_layernorm weight (ones if None)
+    norm_eps: float = 1e-6
+    correction_bias: Optional[torch.Tensor] = None  # [E] fp32, DeepSeek-V3 (noaux_tc) router only
 
 
 @dataclass
@@ -94,7 +97,8 @@ class MoELayer:
     def __init__(self, params: LayerParams, placement: Placement, top_k: int, norm_topk_prob: bool,
                  rank: int = 0, comm: Optional[GroupCommunicator] = None,
                  routed_scaling_factor: float = 1.0, shared_gate: bool = False,
-                 status: Optional[torch.Tensor] = None):
+                 status: Optional[torch.Tensor] = None, scoring: str = "softmax",
+                 n_group: int = 1, topk_group: int = 1):
         self.p = params
         self.placement = placement
         self.top_k = top_k
@@ -103,6 +107,11 @@ class MoELayer:
         self.comm = comm
         self.scale = routed_scaling_factor
         self.shared_gate = shared_gate
+        if scoring not in ("softmax", "sigmoid_grouped"):
+            raise ValueError(f"unknown scoring {scoring!r}")
+        if scoring == "sigmoid_grouped" and (params.correction_bias is None or shared_gate):
+            raise ValueError("sigmoid_grouped routing needs correction_bias and no shared-gate column")
+        self.scoring, self.n_group, self.topk_group = scoring, n_group, topk_group
         self.G, self.P = placement.ep_size, placement.slots_per_rank
         self.E = placement.num_logical
         self.H = params.w_gate_up.shape[2]
@@ -114,6 +123,9 @@ class MoELayer:
         self.ws = ops.Workspace(dev)
         self.status = status
         self._shared_offsets = {}
+        self._normed = {}
+        if params.norm_weight is None:
+            params.norm_weight = torch.ones(self.H, dtype=params.gate_w.dtype, device=dev)
         if params.gate_w.shape[0] != self.E + (1 if shared_gate else 0):
             raise ValueError("gate_w rows must be E (+1 with a shared-expert gate)")
 
@@ -121,12 +133,19 @@ class MoELayer:
     def route_and_permute(self, x: torch.Tensor) -> DispatchState:
         T = x.shape[0]
         E1 = self.p.gate_w.shape[0]
-        r = ops.router(x, self.p.gate_w, self.top_k, renorm=self.norm_topk_prob,
-                       gate_bias=self.p.gate_bias, scale=self.scale,
-                       has_shared_gate=self.shared_gate,
-                       log2phy=self.log2phy if self.use_map else None,
-                       rep_count=self.rep_count if self.use_map else None,
-                       num_slots=self.G * self.P, workspace=self.ws, status=self.status)
+        l2p = self.log2phy if self.use_map else None
+        rep = self.rep_count if self.use_map else None
+        if self.scoring == "sigmoid_grouped":
+            r = ops.router_sigmoid_grouped(x, self.p.gate_w, self.p.correction_bias, self.top_k,
+                                           n_group=self.n_group, topk_group=self.topk_group,
+                                           renorm=self.norm_topk_prob, scale=self.scale, log2phy=l2p,
+                                           rep_count=rep, num_slots=self.G * self.P, workspace=self.ws,
+                                           status=self.status)
+        else:
+            r = ops.router(x, self.p.gate_w, self.top_k, renorm=self.norm_topk_prob,
+                           gate_bias=self.p.gate_bias, scale=self.scale,
+                           has_shared_gate=self.shared_gate, log2phy=l2p, rep_count=rep,
+                           num_slots=self.G * self.P, workspace=self.ws, status=self.status)
         perm = ops.permute(x, r, num_slots=self.G * self.P, E1=E1)
         return DispatchState(T=T, route=r, perm=perm)
 
@@ -195,6 +214,19 @@ class MoELayer:
                            shared_gate=st.route.shared_gate, out=out)
 
     # ------------------------------------------------------------ whole layer
+    def forward_block(self, residual: torch.Tensor, hidden: Optional[torch.Tensor] = None,
+                      out: Optional[torch.Tensor] = None,
+                      residual_out: Optional[torch.Tensor] = None):
+        """The block's view of a layer (moe_all2all.py:331-335 then the MoE):
+        residual += hidden; returns (residual, MoE(RMSNorm(residual)))."""
+        key = (residual.shape, residual.dtype)
+        nbuf = self._normed.get(key)
+        if nbuf is None:
+            nbuf = self._normed[key] = torch.empty_like(residual)
+        ro, normed = ops.add_rmsnorm(residual, hidden, self.p.norm_weight, self.p.norm_eps,
+                                     residual_out=residual_out, normed=nbuf)
+        return ro, self.forward(normed, out=out)
+
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Routed output plus the (gated) shared-expert output for this rank's tokens."""
         st = self.route_and_permute(x)

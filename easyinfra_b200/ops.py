@@ -141,6 +141,45 @@ def router(x: torch.Tensor, gate_w: torch.Tensor, top_k: int, *, renorm: bool,
     return RouterOutput(topk_ids, topk_w, phys, counts, offsets, sg, logits, ws)
 
 
+def router_sigmoid_grouped(x: torch.Tensor, gate_w: torch.Tensor, correction_bias: torch.Tensor,
+                           top_k: int, *, n_group: int, topk_group: int, renorm: bool, scale: float,
+                           log2phy: Optional[torch.Tensor] = None, rep_count: Optional[torch.Tensor] = None,
+                           num_slots: Optional[int] = None, keep_logits: bool = False,
+                           workspace: Optional[Workspace] = None,
+                           status: Optional[torch.Tensor] = None) -> RouterOutput:
+    """DeepSeek-V3 router: sigmoid scores + correction bias, group-limited top-k."""
+    _need_cuda(x, gate_w, correction_bias, log2phy, rep_count, status)
+    x = _rows_contig(x)
+    T, H = x.shape
+    E = gate_w.shape[0]
+    if gate_w.dtype != x.dtype or gate_w.shape[1] != H:
+        raise ValueError("gate_w must be [E, H] with x's dtype")
+    gate_w = gate_w.contiguous()
+    correction_bias = correction_bias.to(torch.float32).contiguous()
+    if num_slots is None:
+        num_slots = E
+    dev = x.device
+    topk_ids = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+    topk_w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    phys = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+    counts = torch.empty(num_slots, dtype=torch.int32, device=dev)
+    offsets = torch.empty(num_slots + 1, dtype=torch.int32, device=dev)
+    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if keep_logits else None
+    ws = (workspace or Workspace(dev)).get(router_workspace_bytes(T, E, num_slots))
+    max_rep = 0
+    if log2phy is not None:
+        log2phy = log2phy.to(torch.int32).contiguous()
+        rep_count = rep_count.to(torch.int32).contiguous()
+        max_rep = log2phy.shape[1]
+    _lib.call("b200moe_router_sigmoid_grouped", x.data_ptr(), x.stride(0), _dtype_code(x),
+              gate_w.data_ptr(), correction_bias.data_ptr(), T, H, E, top_k, n_group, topk_group,
+              int(renorm), float(scale), _ptr(log2phy), _ptr(rep_count), max_rep, num_slots,
+              topk_ids.data_ptr(), topk_w.data_ptr(), phys.data_ptr(), counts.data_ptr(),
+              offsets.data_ptr(), _ptr(logits), ws.data_ptr(), ws.numel(), _ptr(status), _stream())
+    _count(2 if T else 0)
+    return RouterOutput(topk_ids, topk_w, phys, counts, offsets, None, logits, ws)
+
+
 def router_from_logits(logits: torch.Tensor, top_k: int, *, renorm: bool, round_bf16: bool,
                        scale: float = 1.0, has_shared_gate: bool = False,
                        log2phy: Optional[torch.Tensor] = None,
@@ -211,8 +250,8 @@ def grouped_swiglu(x: torch.Tensor, expert_offsets: torch.Tensor, w_gate_up: tor
                    status: Optional[torch.Tensor] = None) -> torch.Tensor:
     """act = silu(x Wg^T) * (x Wu^T) per expert segment; x [rows, H] bf16 expert-major."""
     _need_cuda(x, expert_offsets, w_gate_up, status)
-    if x.dtype != torch.bfloat16 or w_gate_up.dtype != torch.bfloat16:
-        raise TypeError("grouped GEMMs take bfloat16 activations and weights")
+    if x.dtype != w_gate_up.dtype or x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("grouped GEMMs take bfloat16 (tensor cores) or float32 activations and weights")
     x = _rows_contig(x)
     P, twoI, H = w_gate_up.shape
     I = twoI // 2
@@ -220,8 +259,12 @@ def grouped_swiglu(x: torch.Tensor, expert_offsets: torch.Tensor, w_gate_up: tor
     offs = expert_offsets.to(torch.int32).contiguous()
     if offs.numel() != P + 1:
         raise ValueError(f"expert_offsets must have P+1={P + 1} entries")
-    act = out if out is not None else torch.empty(x.shape[0], I, dtype=torch.bfloat16,
-                                                  device=x.device)
+    act = out if out is not None else torch.empty(x.shape[0], I, dtype=x.dtype, device=x.device)
+    if x.dtype == torch.float32:
+        _lib.call("b200moe_grouped_swiglu_f32", x.data_ptr(), x.stride(0), x.shape[0], offs.data_ptr(),
+                  P, H, I, w_gate_up.data_ptr(), act.data_ptr(), act.stride(0), _stream())
+        _count(1 if x.shape[0] else 0)
+        return act
     _hook("grouped_swiglu", "start")
     _lib.call("b200moe_grouped_swiglu", x.data_ptr(), x.stride(0), x.shape[0], offs.data_ptr(),
               P, H, I, w_gate_up.data_ptr(), act.data_ptr(), act.stride(0), _ptr(status),
@@ -237,16 +280,21 @@ def grouped_down(act: torch.Tensor, expert_offsets: torch.Tensor, w_down: torch.
                  status: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = act Wd^T per expert segment (optionally scattering rows through out_row_map)."""
     _need_cuda(act, expert_offsets, w_down, out_row_map, status)
-    if act.dtype != torch.bfloat16 or w_down.dtype != torch.bfloat16:
-        raise TypeError("grouped GEMMs take bfloat16 activations and weights")
+    if act.dtype != w_down.dtype or act.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("grouped GEMMs take bfloat16 (tensor cores) or float32 activations and weights")
     act = _rows_contig(act)
     P, H, I = w_down.shape
     w_down = w_down.contiguous()
     offs = expert_offsets.to(torch.int32).contiguous()
-    y = out if out is not None else torch.empty(act.shape[0], H, dtype=torch.bfloat16,
-                                                device=act.device)
+    y = out if out is not None else torch.empty(act.shape[0], H, dtype=act.dtype, device=act.device)
     if out_row_map is not None:
         out_row_map = out_row_map.to(torch.int32).contiguous()
+    if act.dtype == torch.float32:
+        _lib.call("b200moe_grouped_down_f32", act.data_ptr(), act.stride(0), act.shape[0],
+                  offs.data_ptr(), P, H, I, w_down.data_ptr(), y.data_ptr(), y.stride(0),
+                  _ptr(out_row_map), _stream())
+        _count(1 if act.shape[0] else 0)
+        return y
     _hook("grouped_down", "start")
     _lib.call("b200moe_grouped_down", act.data_ptr(), act.stride(0), act.shape[0],
               offs.data_ptr(), P, H, I, w_down.data_ptr(), y.data_ptr(), y.stride(0),
@@ -299,3 +347,29 @@ def gather_segments(src: torch.Tensor, dst: torch.Tensor, src_start: torch.Tenso
               src_start.data_ptr(), dst_start.data_ptr(), length.data_ptr(), length.numel(),
               int(max_rows), _ptr(inverse_map), _stream())
     _count(1 if (length.numel() and max_rows) else 0)
+
+
+def add_rmsnorm(residual: torch.Tensor, hidden: Optional[torch.Tensor], weight: Optional[torch.Tensor],
+                eps: float = 1e-6, *, residual_out: Optional[torch.Tensor] = None,
+                normed: Optional[torch.Tensor] = None, norm: bool = True):
+    """(residual + hidden, weight * rmsnorm(residual + hidden)) in one pass; returns
+    (residual_out, normed or None)."""
+    _need_cuda(residual, hidden, weight, residual_out, normed)
+    residual = _rows_contig(residual)
+    T, H = residual.shape
+    if hidden is not None:
+        hidden = hidden.contiguous()
+        if hidden.shape != residual.shape or hidden.dtype != residual.dtype:
+            raise ValueError("hidden must match residual")
+    ro = residual_out if residual_out is not None else torch.empty_like(residual)
+    nm = None
+    if norm:
+        if weight is None or weight.dtype != residual.dtype or weight.numel() != H:
+            raise ValueError("norm weight must be [H] in the activation dtype")
+        weight = weight.contiguous()
+        nm = normed if normed is not None else torch.empty_like(residual)
+    _lib.call("b200moe_add_rmsnorm", residual.data_ptr(), _ptr(hidden), _ptr(weight) if norm else None,
+              float(eps), T, H, _dtype_code(residual), residual.stride(0), ro.data_ptr(), _ptr(nm),
+              nm.stride(0) if nm is not None else 0, _stream())
+    _count(1 if T else 0)
+    return ro, nm

@@ -103,6 +103,27 @@ B200MOE_API int b200moe_router(const void* x, int64_t ldx, int x_dtype, const vo
                    size_t workspace_bytes, int* status, void* stream);
 
 /*
+ * Router of the DeepSeek-V3 family: fp32 logits x·W_gᵀ, sigmoid scores, choice =
+ * score + correction_bias, keep the topk_group groups (E / n_group consecutive
+ * experts each) with the largest sum of their two best choices, top-K over the
+ * choices of the kept groups (others count as 0.0), weights = the chosen experts'
+ * sigmoid scores, renormalised (+1e-20) when renorm, times scale, rounded to the
+ * activation dtype; then the same replica pick, histogram and offsets as
+ * b200moe_router.  Replaces DeepseekV3MoEGate.forward (easyinfra/models/deepseek_v3/
+ * modeling_deepseek_v3.py:151-203, scoring_func "sigmoid", topk_method "noaux_tc").
+ * Ties go to the lowest group / expert id.  Requires E % n_group == 0,
+ * n_group <= 32, at least 2 experts per group.  Workspace: b200moe_router_workspace_bytes(T, E, num_slots).
+ */
+B200MOE_API int b200moe_router_sigmoid_grouped(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
+                                               const float* correction_bias, int T, int H, int E, int K,
+                                               int n_group, int topk_group, int renorm, float scale,
+                                               const int32_t* log2phy, const int32_t* rep_count, int max_rep,
+                                               int num_slots, int32_t* topk_ids, float* topk_w,
+                                               int32_t* phys_ids, int32_t* slot_counts, int32_t* slot_offsets,
+                                               float* logits_out, void* workspace, size_t workspace_bytes,
+                                               int* status, void* stream);
+
+/*
  * b200moe_router without a workspace argument: it allocates nothing and takes no
  * caller scratch.  No counterpart in the reference (EasyInfra allocates everything
  * through PyTorch).  For callers that cannot allocate device memory: a plugin handed
@@ -179,6 +200,21 @@ B200MOE_API int b200moe_grouped_down(const void* act, int64_t ld_act, int64_t ro
                          const int32_t* out_row_map, int* status, void* stream);
 
 /*
+ * fp32 versions of the two grouped GEMMs (same arguments, fp32 activations, weights
+ * and outputs; CUDA-core fp32 arithmetic, no tensor-core rounding of the inputs).
+ * For fp32 models, whose reference path (NativeMoE.forward_ep,
+ * native_moe.py:56-103) multiplies in fp32.
+ */
+B200MOE_API int b200moe_grouped_swiglu_f32(const float* x, int64_t ldx, int64_t rows_cap,
+                                           const int32_t* expert_offsets, int P, int H, int I,
+                                           const float* w_gate_up, float* act, int64_t ld_act,
+                                           void* stream);
+B200MOE_API int b200moe_grouped_down_f32(const float* act, int64_t ld_act, int64_t rows_cap,
+                                         const int32_t* expert_offsets, int P, int H, int I,
+                                         const float* w_down, float* out, int64_t ldo,
+                                         const int32_t* out_row_map, void* stream);
+
+/*
  * Combine / weighted unpermute: out[t] = sum_k topk_w[t,k] * y[pos_of[t,k]]
  * (+ shared_gate[t] * shared[t] when shared != NULL; gate 1 when shared_gate == NULL),
  * fp32 accumulation, one rounding to the output dtype.  Replaces
@@ -188,6 +224,20 @@ B200MOE_API int b200moe_grouped_down(const void* act, int64_t ld_act, int64_t ro
 B200MOE_API int b200moe_combine(const void* y, int64_t ldy, int dtype, const int32_t* pos_of,
                     const float* topk_w, int T, int K, int H, const void* shared, int64_t lds,
                     const float* shared_gate, void* out, int64_t ldo, void* stream);
+
+/*
+ * MoE block prologue: residual_out = residual + hidden (rounded to the dtype; hidden
+ * may be NULL: no add), normed = weight * rmsnorm(residual_out) with the reference's
+ * rounding points (fp32 statistics, rounded before and after the weight multiply;
+ * normed may be NULL: add only).  Replaces _add_to_residual + post_attention_layernorm
+ * in MoeAll2AllBlock.all2all_chunk_routing_compute (easyinfra/generation/blocks/moe/
+ * moe_all2all.py:331-335; _rmsnorm at generation/modules/rmsnorm/base_rmsnorm.py:6-12).
+ * residual_out may alias residual.
+ */
+B200MOE_API int b200moe_add_rmsnorm(const void* residual, const void* hidden, const void* weight,
+                                    float eps, int T, int H, int dtype, int64_t ld,
+                                    void* residual_out, void* normed, int64_t ld_normed,
+                                    void* stream);
 
 /*
  * Row-segment gather used around the expert-parallel all-to-all: for each segment i,

@@ -5,17 +5,19 @@ Run in a container that has the reference checkout (read-only) at $EASYINFRA_REF
 
     python tests/golden/make_golden.py
 
-It imports the reference's own code on CPU with three shims (the reference targets
-Python 3.14 / torch 2.13; these only make its modules importable here):
+It imports the reference's own code on CPU with import shims (the reference targets
+Python 3.14 / torch 2.13 / transformers 4.57; these only make its modules importable
+here and change none of the code the fixtures run):
   * torch.distributed.all_gather_single is aliased to all_gather_into_tensor
     (generation/parallel/communicator.py:22-25 calls the newer name);
   * TYPE_CHECKING-only annotation names are defined as dummy builtins
     (e.g. generation/modules/moe/base.py:22), which Python 3.12 evaluates eagerly;
-  * the model files are not imported (they need transformers 4.x internals); the
-    4-line routing of Qwen3MoeSparseMoeBlock._routing (models/qwen3_moe/
-    modeling_qwen3_moe.py:255-266) is driven through the reference's BaseLinear and
-    torch ops exactly as written there.
-Then, per case and per simulated rank, it calls
+  * module-level names that the model files import from transformers 4.x /
+    accelerate and that this environment lacks are defined as inert placeholder
+    classes (import time only), so Qwen3MoeSparseMoeBlock and DeepseekV3MoEGate
+    import and their own routing code runs.
+Then, per case and per simulated rank, it calls Qwen3MoeSparseMoeBlock._routing
+(models/qwen3_moe/modeling_qwen3_moe.py:255-266) through
   MoeAll2AllBlock.all2all_chunk_routing_compute (routing glue, EPLB pick, counts,
       sort/permute; blocks/moe/moe_all2all.py:325-373),
   NativeMoE.forward_ep (modules/moe/native_moe.py:56-103),
@@ -51,6 +53,36 @@ from easyinfra_b200 import configs as C  # noqa: E402
 from tests.golden import cases  # noqa: E402
 
 
+def _import_with_placeholders(modname: str, names):
+    """Import `names` from `modname`; every module-level name that the reference
+    imports from transformers 4.x / accelerate and that this environment lacks is
+    defined as an inert placeholder class (import-time only: none of them is used by
+    the routing functions these fixtures call).  Returns the placeholders made."""
+    import importlib
+    import re
+    made = []
+    for _ in range(400):
+        try:
+            mod = importlib.import_module(modname)
+            return [getattr(mod, n) for n in names], made
+        except ImportError as e:
+            msg = str(e)
+            m = re.search(r"cannot import name '(\w+)' from '([\w\.]+)'", msg)
+            m2 = re.search(r"No module named '([\w\.]+)'", msg)
+            if m:
+                target = importlib.import_module(m.group(2))
+                setattr(target, m.group(1), type(m.group(1), (), {"__init__": lambda self, *a, **k: None}))
+                made.append(f"{m.group(2)}.{m.group(1)}")
+            elif m2:
+                sys.modules[m2.group(1)] = types.ModuleType(m2.group(1))
+                made.append(m2.group(1))
+            else:
+                raise
+            for k in [k for k in sys.modules if k.startswith("easyinfra.models")]:
+                del sys.modules[k]
+    raise RuntimeError("could not import " + modname)
+
+
 def import_reference():
     if not hasattr(dist, "all_gather_single"):
         dist.all_gather_single = dist.all_gather_into_tensor
@@ -60,6 +92,11 @@ def import_reference():
     os.environ.setdefault("MOE_IMPL", "native")
     os.environ.setdefault("CLASS_TIMING_MODE", "0")
     sys.path.insert(0, REF)
+    (Qwen3Block,), made = _import_with_placeholders(
+        "easyinfra.models.qwen3_moe.modeling_qwen3_moe", ["Qwen3MoeSparseMoeBlock"])
+    (DSGate,), made2 = _import_with_placeholders(
+        "easyinfra.models.deepseek_v3.modeling_deepseek_v3", ["DeepseekV3MoEGate"])
+    print(f"import placeholders: {len(made) + len(made2)}")
     from easyinfra.generation.modules.moe.native_moe import NativeMoE
     from easyinfra.generation.blocks.moe.base import _MoeBlock, eplb_map_to_physical_and_record
     from easyinfra.generation.blocks.moe.moe_all2all import MoeAll2AllBlock
@@ -68,7 +105,7 @@ def import_reference():
     from easyinfra.generation.modules.moe.eplb.eplb import rebalance_experts
     return NS(NativeMoE=NativeMoE, MoeBlock=_MoeBlock, All2All=MoeAll2AllBlock, MlpBlock=MlpBlock,
               BaseLinear=BaseLinear, eplb_pick=eplb_map_to_physical_and_record,
-              rebalance_experts=rebalance_experts)
+              rebalance_experts=rebalance_experts, Qwen3Block=Qwen3Block, DSGate=DSGate)
 
 
 def checksum(t: torch.Tensor) -> str:
@@ -121,16 +158,10 @@ def make_block_self(R, shape, P, G, rank, phy2log, use_eplb, gate, shared_mlp):
     s.logical_replica_count = rep
     s.local_expert_mask_retriever = torch.arange(G * P).view(G, P)
 
-    def _routing(hidden_states):
-        # modeling_qwen3_moe.py:255-266, verbatim semantics
-        routing_weights = torch.nn.functional.softmax(gate(hidden_states), dim=-1, dtype=torch.float)
-        routing_weights, selected_experts = torch.topk(routing_weights, shape.top_k, dim=-1)
-        if shape.norm_topk_prob:
-            routing_weights = routing_weights / routing_weights.sum(dim=-1, keepdim=True)
-        routing_weights = routing_weights.to(hidden_states.dtype)
-        return routing_weights, selected_experts, None
-
-    s._routing = _routing
+    # the reference's own router: Qwen3MoeSparseMoeBlock._routing
+    # (models/qwen3_moe/modeling_qwen3_moe.py:255-266) bound to this stand-in
+    s.gate = gate
+    s._routing = types.MethodType(R.Qwen3Block._routing, s)
     s._chunk_routing_compute = types.MethodType(R.MoeBlock._chunk_routing_compute, s)
     s._all_expert_count_compute = types.MethodType(R.MoeBlock._all_expert_count_compute, s)
     s.get_shared_experts = lambda: shared_mlp
@@ -254,8 +285,45 @@ def make_qwen15_map(R, layers=24, G=8, slots=64):
     return {"phy2log": phy2log.tolist()}
 
 
+DSV3_CASES = {
+    # Moonlight-16B-A3B-like (the reference ships its EPLB maps): 64 experts, 1 group
+    "dsv3_moonlight": dict(E=64, n_group=1, topk_group=1, K=6, scale=2.446, H=256, T=96),
+    # DeepSeek-V3-like grouping: 256 experts in 8 groups, 4 groups kept, top-8
+    "dsv3_v3": dict(E=256, n_group=8, topk_group=4, K=8, scale=2.5, H=256, T=96),
+}
+
+
+def dsv3_inputs(c):
+    """Seeded inputs of a DeepSeek-V3 gate case: x [T,H] bf16, W [E,H] bf16,
+    e_score_correction_bias [E] fp32."""
+    g = torch.Generator().manual_seed(1000 + c["E"] + c["n_group"])
+    x = torch.randn(c["T"], c["H"], generator=g).to(torch.bfloat16)
+    w = (torch.randn(c["E"], c["H"], generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(c["E"], generator=g) * 0.05).float()
+    return x, w, b
+
+
+def run_dsv3_case(R, c):
+    cfg = NS(num_experts_per_tok=c["K"], n_routed_experts=c["E"], routed_scaling_factor=c["scale"],
+             scoring_func="sigmoid", seq_aux=True, topk_method="noaux_tc", n_group=c["n_group"],
+             topk_group=c["topk_group"], norm_topk_prob=True, hidden_size=c["H"])
+    gate = R.DSGate(cfg).eval()
+    x, w, b = dsv3_inputs(c)
+    with torch.no_grad():
+        gate.weight = torch.nn.Parameter(w.float(), requires_grad=False)
+        gate.e_score_correction_bias = torch.nn.Parameter(b, requires_grad=False)
+        topk_w, topk_idx, _ = R.DSGate.forward(gate, x)   # modeling_deepseek_v3.py:151-203
+        logits = torch.nn.functional.linear(x.float(), w.float())
+    return {"logits": logits.numpy(), "ids": topk_idx.numpy(), "weights": topk_w.float().numpy(),
+            "meta_json": np.frombuffer(json.dumps({"case": c}).encode(), dtype=np.uint8)}
+
+
 def main():
     R = import_reference()
+    for name, c in DSV3_CASES.items():
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **run_dsv3_case(R, c))
+        print(f"{name}: {os.path.getsize(path) / 1024:.0f} KiB")
     os.makedirs(C.DATA_DIR, exist_ok=True)
     qmap = make_qwen15_map(R)
     with open(os.path.join(C.DATA_DIR, "qwen15-64-slots-8.json"), "w") as f:

@@ -54,10 +54,14 @@ def build(case, device, dtype=None):
     return shape, layers, lw, phy2log, xs
 
 
-@pytest.mark.parametrize("name", [n for n in cases.CASES if n != "c1"])
+@pytest.mark.parametrize("name", list(cases.CASES))
 def test_layer_matches_oracle(cuda_device, name):
+    """bf16 cases: <= 6e-3 vs the fp32-accumulate oracle, 1e-2 vs the reference's
+    numerics; config 1 (fp32 end to end): <= 1e-5 vs the reference's fp32 path."""
     case = cases.CASES[name]
     shape, layers, lw, phy2log, xs = build(case, cuda_device)
+    fp32 = shape.dtype == torch.float32
+    tight_tol, spec_tol = (1e-5, 1e-5) if fp32 else (TIGHT_TOL, SPEC_TOL)
     outs, sts = forward_ep_single_device(layers, [x.to(cuda_device) for x in xs], return_states=True)
     torch.cuda.synchronize()
     ref_tight = O.moe_layer_ep(xs, lw, shape.top_k, shape.norm_topk_prob, phy2log,
@@ -90,7 +94,7 @@ def test_layer_matches_oracle(cuda_device, name):
         ref_self = float((exp_s - exact).abs().max() / scale)
         print(f"{name} rank {r}: vs fp32-acc {err_tight:.2e}, vs reference {err_spec:.2e}, "
               f"reference vs fp32 {ref_self:.2e}")
-        assert err_tight < TIGHT_TOL, (name, r)
-        assert err_spec < max(SPEC_TOL, ref_self + 2.0 ** -8), (name, r)
+        assert err_tight < tight_tol, (name, r)
+        assert err_spec < (spec_tol if fp32 else max(spec_tol, ref_self + 2.0 ** -8)), (name, r)
     assert mism <= max(1, 0.02 * total), f"{mism}/{total} tokens routed differently"
     print(f"{name}: {mism}/{total} tokens excluded (1-ulp logit differences)")

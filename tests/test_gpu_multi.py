@@ -1,0 +1,101 @@
+"""Expert-parallel MoE layer across real GPUs with NCCL (marked gpu; skipped with fewer
+than 2 GPUs).  Each rank runs MoELayer.forward with its own tokens and slots; the
+count all-gather and both all-to-alls go through NCCL; every rank's output is
+checked against the CPU oracle's simulation of the same EP layer."""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, case_name, q):
+    import torch.distributed as dist
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120), device_id=dev)
+        from easyinfra_b200 import configs as C
+        from easyinfra_b200.communicator import GroupCommunicator
+        from easyinfra_b200.layer import LayerParams, MoELayer
+        from easyinfra_b200.placement import Placement
+        from oracle import moe_oracle as O
+        from tests.golden import cases
+
+        case = dict(cases.CASES[case_name])
+        shape = case["shape"]
+        phy2log = cases.case_phy2log(case)
+        if phy2log.shape[0] != world:
+            phy2log = phy2log.reshape(world, -1)
+        pl = Placement(phy2log, shape.num_experts)
+        P = pl.slots_per_rank
+        gw = C.router_weight(shape, 0)
+        gb = C.gate_bias(shape, 0)
+        sgu, sd = C.shared_weights(shape, 0)
+        wgu_all, wd_all = C.expert_weights(shape, 0, phy2log.reshape(-1).tolist())
+        params = LayerParams(gw.to(dev), wgu_all[rank * P:(rank + 1) * P].to(dev),
+                             wd_all[rank * P:(rank + 1) * P].to(dev),
+                             None if gb is None else gb.to(shape.dtype).float().to(dev),
+                             None if sgu is None else sgu.to(dev), None if sd is None else sd.to(dev))
+        comm = GroupCommunicator(group=dist.group.WORLD)
+        lay = MoELayer(params, pl, shape.top_k, shape.norm_topk_prob, rank=rank, comm=comm,
+                       shared_gate=shape.shared_gate)
+        T = case["T"]
+        xs = [C.hidden_states(shape, T, rank=r) for r in range(world)]
+        out = lay.forward(xs[rank].to(dev))
+        out2 = lay.forward(xs[rank].to(dev))     # second call: buffers and tables reused
+        torch.cuda.synchronize()
+        st = lay.route_and_permute(xs[rank].to(dev))
+        ids = st.route.topk_ids.cpu().long()
+        lw = O.LayerWeights(gw[:shape.num_experts], wgu_all, wd_all,
+                            None if gb is None else gb.to(shape.dtype), sgu, sd,
+                            gw[shape.num_experts] if shape.shared_gate else None)
+        ref = O.moe_layer_ep(xs, lw, shape.top_k, shape.norm_topk_prob, phy2log,
+                             use_eplb=not pl.is_identity, fp32_accumulate=True)
+        same = (ids == ref[rank].ids).all(-1)
+        exp = O.layer_output(ref[rank]).float()[same]
+        err = float((out.cpu().float()[same] - exp).abs().max() / exp.abs().max())
+        rep = bool(torch.equal(out, out2))
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+        q.put((rank, err, int((~same).sum()), rep, None))
+    except Exception:
+        q.put((rank, None, None, None, traceback.format_exc()))
+
+
+@pytest.mark.parametrize("case_name", ["mixtral_g2", "qwen3_g8", "dsv2_g2"])
+def test_ep_layer_over_nccl(case_name):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case_name, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, err, excluded, rep, tb in res:
+        assert tb is None, f"rank {rank}:\n{tb}"
+        assert err < 6e-3, (rank, err)
+        assert rep, "two calls of the same layer gave different outputs"
+        assert excluded <= 2

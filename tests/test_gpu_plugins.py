@@ -76,9 +76,7 @@ def test_block_stages_ep1_match_oracle(cuda_device):
     torch.cuda.synchronize()
     res_out, hid_out = chunk.active_variables
     # oracle: residual add, RMSNorm (weight 1), MoE on the normed input
-    r = residual + hidden
-    f = r.float()
-    normed = (f * torch.rsqrt(f.pow(2).mean(-1, keepdim=True) + 1e-6)).to(r.dtype)
+    r, normed = O.add_rmsnorm(residual, hidden, torch.ones(H, dtype=residual.dtype), 1e-6)
     tr = O.moe_layer_ep([normed], O.LayerWeights(gw, wgu, wd, None, sgu, sd), shape.top_k,
                         shape.norm_topk_prob, torch.arange(E).view(1, E), use_eplb=False,
                         fp32_accumulate=True)[0]
