@@ -14,6 +14,15 @@
 
 namespace b200moe {
 
+bool pdl_enabled() {
+  static int cached = -1;
+  if (cached < 0) {
+    const char* v = getenv("B200MOE_PDL");
+    cached = (v != nullptr && v[0] == '0') ? 0 : 1;
+  }
+  return cached == 1;
+}
+
 int num_sms() {
   static int cached[64] = {0};
   int dev = 0;
@@ -33,6 +42,8 @@ __global__ void __launch_bounds__(256) gather_segments_kernel(const uint8_t* src
                                                               const int32_t* dst_start,
                                                               const int32_t* len, int rows_per_cta,
                                                               int32_t* dst_to_src) {
+  pdl_trigger();
+  pdl_wait();
   const int seg = blockIdx.y;
   const int n = len[seg];
   const int r0 = blockIdx.x * rows_per_cta;
@@ -536,9 +547,9 @@ int b200moe_gather_segments(const void* src, void* dst, int64_t row_bytes,
                 static_cast<long long>(row_bytes));
   const int rows_per_cta = 16;
   dim3 grid(static_cast<unsigned>((max_rows + rows_per_cta - 1) / rows_per_cta), static_cast<unsigned>(nseg));
-  gather_segments_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), row_bytes, src_start, dst_start, len,
-      rows_per_cta, dst_to_src);
+  launch_kernel(gather_segments_kernel, grid, dim3(256), 0, static_cast<cudaStream_t>(stream),
+                static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), row_bytes, src_start, dst_start,
+                len, rows_per_cta, dst_to_src);
   return check_launch("gather_segments");
 }
 

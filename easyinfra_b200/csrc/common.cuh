@@ -17,4 +17,27 @@ inline int dtype_bytes(int dt) { return dt == kDtypeBF16 ? 2 : 4; }
 // Multiprocessor count of the current device (cached per device).
 int num_sms();
 
+// Programmatic dependent launch on/off (B200MOE_PDL=0 turns it off).
+bool pdl_enabled();
+
+// Launch `kern` on `stream`, with programmatic stream serialization when enabled.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  cfg.numAttrs = 0;
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 1;
+  }
+  cfg.attrs = attr;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace b200moe

@@ -89,6 +89,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = (p.N + S::OUT_COLS - 1) / S::OUT_COLS;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -108,6 +109,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     tmem_alloc(tmem_holder, S::TMEM_COLS);
     tmem_relinquish();
   }
+  pdl_wait();  // inputs of this launch are complete and visible from here on
   if (warp == 2) {
     int run = 0;
     for (int base = 0; base <= p.P; base += 32) {
@@ -354,7 +356,8 @@ static int run_gemm(const GemmLaunch& L, cudaStream_t stream) {
   const int64_t bound = ((L.rows_cap + BMA - 1) / BMA + L.p.P) * static_cast<int64_t>(nt);
   const int grid = static_cast<int>(bound < num_sms() ? bound : num_sms());
   if (grid <= 0) return 0;
-  grouped_gemm_kernel<BN, STAGES, SWIGLU, BMA><<<grid, GM_THREADS, smem, stream>>>(ma, mb, L.p);
+  launch_kernel(grouped_gemm_kernel<BN, STAGES, SWIGLU, BMA>, dim3(grid), dim3(GM_THREADS), smem, stream, ma, mb,
+                L.p);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

@@ -22,6 +22,8 @@ __global__ void __launch_bounds__(256) grouped_gemm_f32_kernel(GemmF32Params p) 
   __shared__ float Bs[F32_TK][F32_TN + 4];
   __shared__ float Us[SWIGLU ? F32_TK : 1][F32_TN + 4];
   __shared__ int s_e, s_m0;
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0) {
     // m-tile blockIdx.y -> (expert, first row)
     int tile = blockIdx.y, e = -1, m0 = 0;
@@ -94,9 +96,9 @@ int launch_grouped_gemm_f32(const GemmF32Params& p, bool swiglu, cudaStream_t st
   if (p.rows_cap == 0) return 0;
   dim3 grid((p.N + F32_TN - 1) / F32_TN, static_cast<unsigned>((p.rows_cap + F32_TM - 1) / F32_TM + p.P));
   if (swiglu)
-    grouped_gemm_f32_kernel<true><<<grid, 256, 0, stream>>>(p);
+    launch_kernel(grouped_gemm_f32_kernel<true>, grid, dim3(256), 0, stream, p);
   else
-    grouped_gemm_f32_kernel<false><<<grid, 256, 0, stream>>>(p);
+    launch_kernel(grouped_gemm_f32_kernel<false>, grid, dim3(256), 0, stream, p);
   return 0;
 }
 

@@ -76,6 +76,7 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = (p.N + S::FEAT - 1) / S::FEAT;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -95,6 +96,7 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
     tmem_alloc(tmem_holder, S::TMEM_COLS);
     tmem_relinquish();
   }
+  pdl_wait();  // inputs of this launch are complete and visible from here on
   if (warp == 2) {
     for (int base = 0; base <= p.P; base += 32) {
       const int e = base + lane;
@@ -277,7 +279,8 @@ static int run_wm(const GemmLaunch& L, cudaStream_t stream) {
   const int64_t bound = ((L.rows_cap + NTOK - 1) / NTOK + L.p.P) * static_cast<int64_t>(nt);
   const int grid = static_cast<int>(bound < num_sms() ? bound : num_sms());
   if (grid <= 0) return 0;
-  grouped_gemm_wm_kernel<NTOK, STAGES, SWIGLU><<<grid, WM_THREADS, smem, stream>>>(mw, mx, L.p);
+  launch_kernel(grouped_gemm_wm_kernel<NTOK, STAGES, SWIGLU>, dim3(grid), dim3(WM_THREADS), smem, stream, mw,
+                mx, L.p);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

@@ -35,6 +35,8 @@ constexpr int NORM_MAXV = 8;   // rows up to 256 * 8 * 16 B = 32 KB (H <= 16384 
 template <typename E>
 __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(AddNormParams p) {
   __shared__ float red[NORM_THREADS / 32];
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x;
   const E* res = static_cast<const E*>(p.residual) + t * p.ld;
@@ -99,9 +101,9 @@ int launch_add_rmsnorm(const AddNormParams& p, cudaStream_t stream) {
   const int vec = 16 / (p.dtype == kDtypeBF16 ? 2 : 4);
   if (p.H / vec > NORM_THREADS * NORM_MAXV) return -1;
   if (p.dtype == kDtypeBF16)
-    add_rmsnorm_kernel<__nv_bfloat16><<<p.T, NORM_THREADS, 0, stream>>>(p);
+    launch_kernel(add_rmsnorm_kernel<__nv_bfloat16>, dim3(p.T), dim3(NORM_THREADS), 0, stream, p);
   else
-    add_rmsnorm_kernel<float><<<p.T, NORM_THREADS, 0, stream>>>(p);
+    launch_kernel(add_rmsnorm_kernel<float>, dim3(p.T), dim3(NORM_THREADS), 0, stream, p);
   return 0;
 }
 

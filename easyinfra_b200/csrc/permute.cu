@@ -26,6 +26,8 @@ constexpr int PM_MAX_ENTRIES = 64 * 8;  // tb * K must not exceed this
 __global__ void __launch_bounds__(256) permute_rows(PermuteParams p) {
   extern __shared__ int32_t running[];     // [num_slots], -1 == not yet touched
   __shared__ int32_t pos[PM_MAX_ENTRIES];  // destination row of each entry of this block
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * p.tb;
   const int nt = min(p.tb, p.T - t0);
@@ -121,6 +123,8 @@ __device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
 // before any arithmetic, so a token's gathers are in flight together.
 template <typename E>
 __global__ void __launch_bounds__(256) combine_rows(CombineParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int chunks = (p.H + 255) / 256;
@@ -160,7 +164,7 @@ __global__ void __launch_bounds__(256) combine_rows(CombineParams p) {
 int launch_permute(const PermuteParams& p, cudaStream_t stream) {
   if (p.T == 0) return 0;
   const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t);
-  permute_rows<<<p.nblocks, 256, smem, stream>>>(p);
+  launch_kernel(permute_rows, dim3(p.nblocks), dim3(256), smem, stream, p);
   return 0;
 }
 
@@ -169,9 +173,9 @@ int launch_combine(const CombineParams& p, cudaStream_t stream) {
   const int64_t warps = static_cast<int64_t>(p.T) * ((p.H + 255) / 256);
   const int grid = static_cast<int>((warps * 32 + 255) / 256);
   if (p.dtype == kDtypeBF16)
-    combine_rows<__nv_bfloat16><<<grid, 256, 0, stream>>>(p);
+    launch_kernel(combine_rows<__nv_bfloat16>, dim3(grid), dim3(256), 0, stream, p);
   else
-    combine_rows<float><<<grid, 256, 0, stream>>>(p);
+    launch_kernel(combine_rows<float>, dim3(grid), dim3(256), 0, stream, p);
   return 0;
 }
 

@@ -220,6 +220,15 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16_f32(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels are launched with programmatic stream serialization: a kernel may start
+// while its predecessor drains.  Every kernel therefore calls pdl_wait() before its
+// first read or write of global memory that another kernel produces or consumes;
+// pdl_trigger() lets the successor's launch begin early.  Both are no-ops when the
+// kernel was launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));

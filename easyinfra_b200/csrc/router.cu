@@ -34,6 +34,9 @@ constexpr int RL_MAXNT = 17;     // up to 136 logit columns per pass
 
 __global__ void __launch_bounds__(128) router_logits_bf16(RouterLogitsParams p, int cols_per_cta) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  pdl_trigger();
+  pdl_wait();
+
   const int col0 = blockIdx.y * cols_per_cta;
   const int ncols = min(cols_per_cta, p.E1 - col0);
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);     // [64][RL_LD]
@@ -119,6 +122,8 @@ constexpr int RG = 8;
 template <typename E>
 __global__ void __launch_bounds__(256) router_logits_gemv(RouterLogitsParams p) {
   __shared__ float red[8][RG];
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.y, t0 = blockIdx.x * RG;
   const int nt = min(RG, p.T - t0);
@@ -165,6 +170,8 @@ __global__ void __launch_bounds__(256) router_logits_gemv(RouterLogitsParams p) 
 // ------------------------------------------------------------------ logits (fp32)
 // One warp per token; lanes stride over the hidden dimension; 8 experts per pass.
 __global__ void __launch_bounds__(256) router_logits_f32(RouterLogitsParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= p.T) return;
   const float* x = static_cast<const float*>(p.x) + warp * p.ldx;
@@ -203,6 +210,8 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
 __global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
   extern __shared__ int32_t hist[];  // [num_slots], then (scoring 1) 8 warps x 256 floats
   __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
   float* cbuf = reinterpret_cast<float*>(hist + p.num_slots) + (threadIdx.x >> 5) * 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) hist[s] = 0;
@@ -465,9 +474,9 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
   if (p.T <= 256) {
     const dim3 grid((p.T + RG - 1) / RG, p.E1);
     if (x_dtype == kDtypeBF16)
-      router_logits_gemv<__nv_bfloat16><<<grid, 256, 0, stream>>>(p);
+      launch_kernel(router_logits_gemv<__nv_bfloat16>, grid, dim3(256), 0, stream, p);
     else
-      router_logits_gemv<float><<<grid, 256, 0, stream>>>(p);
+      launch_kernel(router_logits_gemv<float>, grid, dim3(256), 0, stream, p);
     return 0;
   }
   if (x_dtype == kDtypeBF16) {
@@ -477,10 +486,10 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
     while (cols > 8 && tok_blocks * ((p.E1 + cols - 1) / cols) < 2 * num_sms()) cols -= 8;
     dim3 grid(tok_blocks, (p.E1 + cols - 1) / cols);
     const size_t smem = static_cast<size_t>(RL_TOK + cols) * RL_LD * sizeof(__nv_bfloat16);
-    router_logits_bf16<<<grid, 128, smem, stream>>>(p, cols);
+    launch_kernel(router_logits_bf16, grid, dim3(128), smem, stream, p, cols);
   } else {
     const int grid = (p.T * 32 + 255) / 256;
-    router_logits_f32<<<grid, 256, 0, stream>>>(p);
+    launch_kernel(router_logits_f32, dim3(grid), dim3(256), 0, stream, p);
   }
   return 0;
 }
@@ -489,7 +498,7 @@ int launch_router_select(const RouterSelectParams& p, cudaStream_t stream) {
   if (p.T == 0) return 0;
   const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t) +
                       (p.scoring == 1 ? 8 * 256 * sizeof(float) : 0);
-  router_select<<<p.nblocks, 256, smem, stream>>>(p);
+  launch_kernel(router_select, dim3(p.nblocks), dim3(256), smem, stream, p);
   return 0;
 }
 
