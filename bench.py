@@ -60,6 +60,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (invalid as a result)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--transport", default="nvlink", choices=["nvlink", "nccl"],
+                    help="expert-parallel row exchange for --gpus > 1: peer memory (graph-captured) "
+                         "or NCCL all_to_all_single (the reference's, host sync per layer)")
     return ap.parse_args()
 
 
@@ -228,6 +231,19 @@ def run_ours(args):
     n_layers = args.layers or shape.num_layers
     shape, layers = build_stack(cfg_key, rank, world, device, group, n_layers)
     hbm, bf16_burst, bf16_sus, peak_kind = peaks()
+    xg = None
+    xg_status = torch.zeros(1, dtype=torch.int32, device=device)
+    if world > 1 and args.transport == "nvlink":
+        from easyinfra_b200.peer_exchange import PeerExchange
+        wls = [args.workload] + ([] if args.no_secondary else SECONDARY.get(args.workload, []))
+        max_t = max(WORKLOADS[w][2] for w in wls if WORKLOADS[w][0] == cfg_key)
+        lay0 = layers[0]
+        xg = PeerExchange.create(group, rank=rank, world_size=world, slots_per_rank=lay0.P, hidden=lay0.H,
+                                 inter=lay0.I, dtype=shape.dtype, max_tokens=max_t, top_k=shape.top_k,
+                                 device=device, timeout_s=10.0, status=xg_status)
+        for lay in layers:
+            lay.exchange = xg
+    use_graph = world == 1 or xg is not None
 
     def barrier():
         if world > 1:
@@ -270,8 +286,9 @@ def run_ours(args):
                 ev.append(e)
 
         ops.LAUNCHES["count"] = 0
-        if world == 1:
-            # one rank: the stack never syncs with the host -> one CUDA graph per step
+        if use_graph:
+            # one rank, or EP over peer memory: the stack never syncs with the host ->
+            # one CUDA graph per rank and step
             def arm():
                 ops.LAUNCHES["count"] = 0   # count the captured forward only, not the warm-ups
                 if with_roofline:
@@ -289,7 +306,7 @@ def run_ours(args):
         sampler = ClockSampler(local_rank) if with_roofline else None
         barrier()
         torch.cuda.synchronize()
-        if world > 1:
+        if not use_graph:
             ops.LAUNCHES["count"] = 0
             ops.EVENT_HOOK["fn"] = hook if with_roofline else None
         t0 = torch.cuda.Event(enable_timing=True)
@@ -313,7 +330,7 @@ def run_ours(args):
         # e2e: host buffers, H2D of the input and D2H of the result inside the region
         xh = x.cpu().pin_memory()
         oh = torch.empty_like(xh).pin_memory()
-        xd = graph.input if world == 1 else torch.empty_like(x)
+        xd = graph.input if use_graph else torch.empty_like(x)
         for _ in range(args.warmup):
             xd.copy_(xh, non_blocking=True)
             oh.copy_(run(xd), non_blocking=True)
@@ -333,7 +350,9 @@ def run_ours(args):
         res = {"workload": wl_name, "T": T, "ms": ms, "value": tok / (ms / 1e3),
                "e2e_value": tok / (e2e_ms / 1e3), "e2e_ms": e2e_ms,
                "h2d": xh.numel() * xh.element_size() * world, "d2h": oh.numel() * oh.element_size() * world,
-               "launches": launches, "clocks": clocks, "graph": world == 1}
+               "launches": launches, "clocks": clocks, "graph": use_graph}
+        if use_graph:
+            del graph, run
         if with_roofline and kernel_ms and layer_rows[0] is not None:
             # algorithmic work of the SwiGLU GEMM per launch, averaged over layers
             H, I = shape.hidden, shape.intermediate
@@ -369,6 +388,9 @@ def run_ours(args):
         ts = [run(n) for _ in range(3)]
         cpu = {"value": n / statistics.median(ts), "unit": UNIT, "cores": cores, "kind": "port",
                "sample": sample}
+    exchange_status = int(max_over_ranks(float(xg_status.item()))) if world > 1 else 0
+    if xg is not None:
+        xg.close(group)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -381,7 +403,8 @@ def run_ours(args):
         "config": {"workload": f"{shape.name} {args.workload} stack", "layers": len(layers),
                    "tokens_per_rank": main["T"], "hidden": shape.hidden, "experts": shape.num_experts,
                    "top_k": shape.top_k, "intermediate": shape.intermediate,
-                   "parallelism": f"ep{world}", "l2": "inputs larger than L2 (per-layer weights "
+                   "parallelism": f"ep{world}",
+                   "transport": None if world == 1 else args.transport, "l2": "inputs larger than L2 (per-layer weights "
                    f"{3 * shape.hidden * shape.intermediate * 2 * shape.num_experts / 1e9:.2f} GB)"},
         "e2e": {"value": main["e2e_value"], "unit": UNIT, "h2d_bytes_per_step": main["h2d"],
                 "d2h_bytes_per_step": main["d2h"], "ms_per_step": main["e2e_ms"]},
@@ -392,6 +415,8 @@ def run_ours(args):
         "clocks": main["clocks"],
         "secondary": secondary,
     }
+    if exchange_status:
+        line["exchange_status"] = exchange_status   # a bounded wait gave up: numbers invalid
     if args.layers:
         line["config"]["debug_reduced_layers"] = True
     print(json.dumps(line), flush=True)

@@ -68,6 +68,16 @@ SIGNATURES = {
         [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
          c_int64, c_void_p, c_void_p, c_void_p],
     ),
+    "b200moe_grouped_swiglu_ex": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
+         c_int64, c_void_p, c_void_p],
+    ),
+    "b200moe_grouped_down_ex": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
+         c_int64, c_void_p, c_void_p, c_void_p],
+    ),
     "b200moe_grouped_swiglu_f32": (
         c_int,
         [c_void_p, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int64,
@@ -93,7 +103,36 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_void_p,
          c_void_p],
     ),
+    "b200moe_ep_layout": (
+        c_int, [c_int, c_int, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p]),
+    "b200moe_ep_alloc": (c_int, [c_size_t, c_void_p, c_void_p]),
+    "b200moe_ep_open": (c_int, [c_void_p, c_void_p]),
+    "b200moe_ep_close": (c_int, [c_void_p]),
+    "b200moe_ep_free": (c_int, [c_void_p]),
+    "b200moe_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "b200moe_ep_collect": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "b200moe_ep_combine_send": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "b200moe_ep_wait_combine": (c_int, [c_void_p, c_void_p]),
 }
+
+EP_MAX_RANKS = 8
+EP_HANDLE_BYTES = 64
+
+
+class EpDesc(ctypes.Structure):
+    """b200moe_ep_desc (include/b200moe.h)."""
+    _fields_ = [
+        ("peer", c_void_p * EP_MAX_RANKS),
+        ("world_size", c_int),
+        ("rank", c_int),
+        ("slots_per_rank", c_int),
+        ("row_bytes", c_int),
+        ("cap_rows", c_int64),
+        ("comb_rows", c_int64),
+        ("counters", c_void_p),
+        ("status", c_void_p),
+        ("timeout_ns", ctypes.c_uint64),
+    ]
 
 
 class B200MoEError(RuntimeError):

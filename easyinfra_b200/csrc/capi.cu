@@ -1,8 +1,8 @@
 // C-ABI entry points of libb200moe.so (declared in include/b200moe.h).
 //
 // This layer validates arguments, lays out the router workspace, picks kernel
-// configurations and launches on the caller's stream.  It never allocates device
-// memory and never throws across the ABI.
+// configurations and launches on the caller's stream.  It never throws across the
+// ABI and allocates device memory only in b200moe_ep_alloc (the exchange buffer).
 #include <cstdarg>
 #include <cstdlib>
 #include <cstdio>
@@ -372,6 +372,14 @@ int b200moe_grouped_swiglu(const void* x, int64_t ldx, int64_t rows_cap,
                            const int32_t* expert_offsets, int P, int H, int I,
                            const void* w_gate_up, void* act, int64_t ld_act, int* status,
                            void* stream) {
+  return b200moe_grouped_swiglu_ex(x, ldx, rows_cap, 0, expert_offsets, P, H, I, w_gate_up, act, ld_act,
+                                   status, stream);
+}
+
+int b200moe_grouped_swiglu_ex(const void* x, int64_t ldx, int64_t rows_cap, int64_t rows_hint,
+                              const int32_t* expert_offsets, int P, int H, int I,
+                              const void* w_gate_up, void* act, int64_t ld_act, int* status,
+                              void* stream) {
   int rc;
   if ((rc = device_ok())) return rc;
   if (P < 1 || H <= 0 || I <= 0 || rows_cap < 0) return fail(B200MOE_EINVAL, "P=%d H=%d I=%d", P, H, I);
@@ -398,6 +406,7 @@ int b200moe_grouped_swiglu(const void* x, int64_t ldx, int64_t rows_cap,
   L.p.out_row_map = nullptr;
   L.p.status = status;
   L.variant = gemm_variant_from_env();
+  L.rows_hint = rows_hint < 0 ? 0 : rows_hint;
   rc = launch_grouped_swiglu(L, static_cast<cudaStream_t>(stream));
   if (rc == -4) return fail(B200MOE_EUNSUPPORTED, "P=%d exceeds the kernel's slot limit", P);
   if (rc == -1) return fail(B200MOE_ECUDA, "cuTensorMapEncodeTiled failed (gate_up)");
@@ -409,6 +418,14 @@ int b200moe_grouped_down(const void* act, int64_t ld_act, int64_t rows_cap,
                          const int32_t* expert_offsets, int P, int H, int I,
                          const void* w_down, void* out, int64_t ldo,
                          const int32_t* out_row_map, int* status, void* stream) {
+  return b200moe_grouped_down_ex(act, ld_act, rows_cap, 0, expert_offsets, P, H, I, w_down, out, ldo,
+                                 out_row_map, status, stream);
+}
+
+int b200moe_grouped_down_ex(const void* act, int64_t ld_act, int64_t rows_cap, int64_t rows_hint,
+                            const int32_t* expert_offsets, int P, int H, int I,
+                            const void* w_down, void* out, int64_t ldo,
+                            const int32_t* out_row_map, int* status, void* stream) {
   int rc;
   if ((rc = device_ok())) return rc;
   if (P < 1 || H <= 0 || I <= 0 || rows_cap < 0) return fail(B200MOE_EINVAL, "P=%d H=%d I=%d", P, H, I);
@@ -435,6 +452,7 @@ int b200moe_grouped_down(const void* act, int64_t ld_act, int64_t rows_cap,
   L.p.out_row_map = out_row_map;
   L.p.status = status;
   L.variant = gemm_variant_from_env();
+  L.rows_hint = rows_hint < 0 ? 0 : rows_hint;
   rc = launch_grouped_down(L, static_cast<cudaStream_t>(stream));
   if (rc == -4) return fail(B200MOE_EUNSUPPORTED, "P=%d exceeds the kernel's slot limit", P);
   if (rc == -1) return fail(B200MOE_ECUDA, "cuTensorMapEncodeTiled failed (down)");
@@ -551,6 +569,160 @@ int b200moe_gather_segments(const void* src, void* dst, int64_t row_bytes,
                 static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), row_bytes, src_start, dst_start,
                 len, rows_per_cta, dst_to_src);
   return check_launch("gather_segments");
+}
+
+// ------------------------------------------------------------------ peer exchange
+// counters[0..2]: tickets of dispatch / collect / combine_send; counters[3]: dispatch
+// arrivals consumed; counters[4]: combine arrivals consumed.
+static_assert(sizeof(cudaIpcMemHandle_t) == B200MOE_EP_HANDLE_BYTES, "IPC handle size");
+
+}  // extern "C"
+
+namespace {
+
+int ep_params(const b200moe_ep_desc* ep, EpParams* p) {
+  if (ep == nullptr) return fail(B200MOE_EINVAL, "null exchange descriptor");
+  const int G = ep->world_size;
+  if (G < 1 || G > B200MOE_EP_MAX_RANKS || ep->rank < 0 || ep->rank >= G)
+    return fail(B200MOE_EINVAL, "world_size=%d rank=%d (at most %d ranks)", G, ep->rank, B200MOE_EP_MAX_RANKS);
+  const int P = ep->slots_per_rank;
+  if (P < 1 || ep->row_bytes <= 0 || ep->row_bytes % 16 != 0 || ep->cap_rows < 0 || ep->comb_rows < 0)
+    return fail(B200MOE_EINVAL, "P=%d row_bytes=%d cap_rows=%lld comb_rows=%lld", P, ep->row_bytes,
+                static_cast<long long>(ep->cap_rows), static_cast<long long>(ep->comb_rows));
+  if (static_cast<int64_t>(G) * ep->cap_rows > INT32_MAX || ep->comb_rows > INT32_MAX)
+    return fail(B200MOE_EUNSUPPORTED, "exchange regions above 2^31 rows");
+  if (sizeof(int32_t) * (2 * G * P + G + 1 + P + 1) > 48 * 1024)
+    return fail(B200MOE_EUNSUPPORTED, "G*P=%d too large for the collect kernel's tables", G * P);
+  if (ep->counters == nullptr) return fail(B200MOE_EINVAL, "null counters");
+  for (int g = 0; g < G; ++g) {
+    if (ep->peer[g] == nullptr || !aligned16(ep->peer[g])) return fail(B200MOE_EINVAL, "peer buffer %d", g);
+    p->peer[g] = static_cast<uint8_t*>(ep->peer[g]);
+  }
+  for (int g = G; g < EP_MAX_RANKS; ++g) p->peer[g] = nullptr;
+  p->G = G;
+  p->P = P;
+  p->rank = ep->rank;
+  p->row_bytes = ep->row_bytes;
+  p->cap_rows = ep->cap_rows;
+  p->comb_rows = ep->comb_rows;
+  p->ticket = ep->counters;
+  p->status = ep->status;
+  return B200MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200moe_ep_layout(int world_size, int slots_per_rank, int64_t cap_rows, int64_t comb_rows, int row_bytes,
+                      int64_t* recv_offset, int64_t* comb_offset, int64_t* total_bytes) {
+  if (world_size < 1 || world_size > B200MOE_EP_MAX_RANKS || slots_per_rank < 1 || cap_rows < 0 ||
+      comb_rows < 0 || row_bytes <= 0 || row_bytes % 16 != 0)
+    return fail(B200MOE_EINVAL, "world_size=%d P=%d row_bytes=%d", world_size, slots_per_rank, row_bytes);
+  if (recv_offset) *recv_offset = ep_recv_offset(world_size, slots_per_rank);
+  if (comb_offset) *comb_offset = ep_comb_offset(world_size, slots_per_rank, cap_rows, row_bytes);
+  if (total_bytes) *total_bytes = ep_buffer_bytes(world_size, slots_per_rank, cap_rows, comb_rows, row_bytes);
+  return B200MOE_OK;
+}
+
+int b200moe_ep_alloc(size_t bytes, void** buffer, void* handle) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (bytes == 0 || buffer == nullptr || handle == nullptr) return fail(B200MOE_EINVAL, "ep_alloc arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail(B200MOE_ECUDA, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(B200MOE_ECUDA, "exchange buffer setup: %s", cudaGetErrorString(e));
+  }
+  memcpy(handle, &h, sizeof(h));
+  *buffer = p;
+  return B200MOE_OK;
+}
+
+int b200moe_ep_open(const void* handle, void** peer_buffer) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (handle == nullptr || peer_buffer == nullptr) return fail(B200MOE_EINVAL, "ep_open arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(B200MOE_ECUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  return B200MOE_OK;
+}
+
+int b200moe_ep_close(void* peer_buffer) {
+  if (peer_buffer == nullptr) return B200MOE_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_buffer);
+  if (e != cudaSuccess) return fail(B200MOE_ECUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  return B200MOE_OK;
+}
+
+int b200moe_ep_free(void* buffer) {
+  if (buffer == nullptr) return B200MOE_OK;
+  const cudaError_t e = cudaFree(buffer);
+  if (e != cudaSuccess) return fail(B200MOE_ECUDA, "cudaFree: %s", cudaGetErrorString(e));
+  return B200MOE_OK;
+}
+
+int b200moe_ep_dispatch(const b200moe_ep_desc* ep, const void* send, const int32_t* slot_offsets,
+                        int64_t send_rows, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams p;
+  if ((rc = ep_params(ep, &p))) return rc;
+  if (slot_offsets == nullptr || send_rows < 0 || (send_rows > 0 && (send == nullptr || !aligned16(send))))
+    return fail(B200MOE_EINVAL, "dispatch: send/slot_offsets");
+  if (send_rows > ep->comb_rows)
+    return fail(B200MOE_EINVAL, "send_rows=%lld exceeds comb_rows=%lld", static_cast<long long>(send_rows),
+                static_cast<long long>(ep->comb_rows));
+  p.ticket = ep->counters + 0;
+  if (launch_ep_dispatch(p, send, slot_offsets, send_rows, static_cast<cudaStream_t>(stream)))
+    return fail(B200MOE_ECUDA, "ep_dispatch launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("ep_dispatch");
+}
+
+int b200moe_ep_collect(const b200moe_ep_desc* ep, void* x_expert, int32_t* row_map, int32_t* expert_offsets,
+                       int64_t rows_hint, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams p;
+  if ((rc = ep_params(ep, &p))) return rc;
+  if (x_expert == nullptr || !aligned16(x_expert) || row_map == nullptr || expert_offsets == nullptr)
+    return fail(B200MOE_EINVAL, "collect: null or misaligned output");
+  p.ticket = ep->counters + 1;
+  const int64_t rows = rows_hint > 0 ? rows_hint : static_cast<int64_t>(p.G) * p.cap_rows;
+  if (launch_ep_collect(p, x_expert, row_map, expert_offsets, ep->counters + 3, ep->timeout_ns, rows,
+                        static_cast<cudaStream_t>(stream)))
+    return fail(B200MOE_ECUDA, "ep_collect launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("ep_collect");
+}
+
+int b200moe_ep_combine_send(const b200moe_ep_desc* ep, const void* y_recv, int64_t rows_hint, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams p;
+  if ((rc = ep_params(ep, &p))) return rc;
+  if (y_recv == nullptr || !aligned16(y_recv)) return fail(B200MOE_EINVAL, "combine_send: y_recv");
+  p.ticket = ep->counters + 2;
+  const int64_t rows = rows_hint > 0 ? rows_hint : static_cast<int64_t>(p.G) * p.cap_rows;
+  if (launch_ep_combine_send(p, y_recv, rows, static_cast<cudaStream_t>(stream)))
+    return fail(B200MOE_ECUDA, "ep_combine_send launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("ep_combine_send");
+}
+
+int b200moe_ep_wait_combine(const b200moe_ep_desc* ep, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams p;
+  if ((rc = ep_params(ep, &p))) return rc;
+  if (launch_ep_wait_comb(p, ep->counters + 4, ep->timeout_ns, static_cast<cudaStream_t>(stream)))
+    return fail(B200MOE_ECUDA, "ep_wait_combine launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("ep_wait_combine");
 }
 
 }  // extern "C"

@@ -365,7 +365,10 @@ static int run_gemm(const GemmLaunch& L, cudaStream_t stream) {
 // HBM-bound; the weight-major kernel (grouped_gemm_wm.cu) keeps the most weight
 // bytes in flight.  The token-major kernel with 32-row activation tiles remains
 // available (GemmVariant::kTokenMajorSmallM) for comparison.
-static bool decode_regime(const GemmLaunch& L) { return L.rows_cap <= 48 * static_cast<int64_t>(L.p.P); }
+static bool decode_regime(const GemmLaunch& L) {
+  const int64_t rows = L.rows_hint > 0 ? L.rows_hint : L.rows_cap;
+  return rows <= 48 * static_cast<int64_t>(L.p.P);
+}
 
 int launch_grouped_swiglu(const GemmLaunch& L, cudaStream_t stream) {
   if (L.p.P > GM_MAXP) return -4;

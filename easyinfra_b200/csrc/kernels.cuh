@@ -46,6 +46,115 @@ struct RouterSelectParams {
   const float* correction_bias = nullptr;  // [E]
 };
 
+// ---- expert-parallel exchange over peer memory (ep_nvlink.cu)
+constexpr int EP_MAX_RANKS = 8;
+
+// Every rank's exchange buffer (one peer-mapped allocation per rank, same layout):
+//   [0, 256)            flags: disp[G] then comb[G], u32, only ever incremented
+//   [256, 256 + meta)   meta: G x (P + 1) i32 — per source: rows per local slot, then
+//                       the source's first send row for this rank
+//   recv rows           G x cap_rows rows of row_bytes (region s written by source s)
+//   comb rows           comb_rows rows (this rank's send order, written by the ranks
+//                       that hold its experts)
+struct EpParams {
+  uint8_t* peer[EP_MAX_RANKS];  // base of every rank's buffer (peer[rank] is this rank's)
+  int G, P, rank;
+  int row_bytes;
+  int64_t cap_rows;   // rows per source region
+  int64_t comb_rows;  // rows of the combine region
+  uint32_t* ticket;   // local, zero between launches
+  int* status;
+};
+
+__host__ __device__ inline int64_t ep_meta_bytes(int G, int P) {
+  return ((static_cast<int64_t>(G) * (P + 1) * 4 + 255) / 256) * 256;
+}
+__host__ __device__ inline int64_t ep_recv_offset(int G, int P) { return 256 + ep_meta_bytes(G, P); }
+__host__ __device__ inline int64_t ep_comb_offset(int G, int P, int64_t cap_rows, int row_bytes) {
+  return ep_recv_offset(G, P) + static_cast<int64_t>(G) * cap_rows * row_bytes;
+}
+__host__ __device__ inline int64_t ep_buffer_bytes(int G, int P, int64_t cap_rows, int64_t comb_rows,
+                                                   int row_bytes) {
+  return ep_comb_offset(G, P, cap_rows, row_bytes) + comb_rows * row_bytes;
+}
+__device__ __forceinline__ uint32_t* ep_flags(uint8_t* base) { return reinterpret_cast<uint32_t*>(base); }
+__device__ __forceinline__ int32_t* ep_meta(uint8_t* base, const EpParams& p) {
+  return reinterpret_cast<int32_t*>(base + 256);
+}
+__device__ __forceinline__ uint8_t* ep_recv_rows(uint8_t* base, const EpParams& p) {
+  return base + ep_recv_offset(p.G, p.P);
+}
+__device__ __forceinline__ uint8_t* ep_comb_rows(uint8_t* base, const EpParams& p) {
+  return base + ep_comb_offset(p.G, p.P, p.cap_rows, p.row_bytes);
+}
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait for *flag >= target (wrap-safe compare); false on timeout.  A zero
+// timeout checks once, and so does every wait once the status word holds an error
+// (a layer that already failed drains instead of waiting out every later limit).
+__device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t target, uint64_t timeout_ns,
+                                              const int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (static_cast<int32_t>(ld_acquire_sys(flag) - target) >= 0) return true;
+    if (timeout_ns == 0 || globaltimer_ns() - t0 > timeout_ns) return false;
+    if (status != nullptr && *reinterpret_cast<const volatile int*>(status) != 0) return false;
+    __nanosleep(64);
+  }
+}
+
+// One warp copies one row; L2-only loads for rows that a peer wrote.
+template <bool FROM_PEER>
+__device__ __forceinline__ void copy_row(uint8_t* dst, const uint8_t* src, int row_bytes, int lane) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  const int n = row_bytes >> 4;
+  for (int v = lane; v < n; v += 32) d[v] = FROM_PEER ? __ldcg(s + v) : s[v];
+}
+
+// Clamp a per-slot count so that the running sum never exceeds `cap`.
+__device__ __forceinline__ int clamp_run(int cnt, int run, int64_t cap) {
+  const int64_t room = cap - run;
+  return static_cast<int>(max64(0, min64(cnt, room)));
+}
+
+// True in the last CTA of the grid to get here (ticket), after every thread of every
+// CTA fenced its stores at system scope.
+__device__ __forceinline__ bool last_cta(uint32_t* ticket, int* s_last) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) *s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+  __syncthreads();
+  return *s_last != 0;
+}
+
+// Run by thread d (< G) of the last CTA once every row for destination d is stored and
+// fenced: d's metadata for this source (rows per slot of d clamped to cap_rows, then
+// this source's first send row for d), a system fence, then d.disp[rank] += 1.
+// Thread 0 also resets the ticket.
+__device__ __forceinline__ void ep_publish_dispatch(const EpParams& p, const int32_t* slot_offsets, int d) {
+  const int P = p.P;
+  int32_t* meta = ep_meta(p.peer[d], p) + p.rank * (P + 1);
+  int run = 0;
+  for (int q = 0; q < P; ++q) {
+    const int c = clamp_run(slot_offsets[d * P + q + 1] - slot_offsets[d * P + q], run, p.cap_rows);
+    meta[q] = c;
+    run += c;
+  }
+  meta[P] = slot_offsets[d * P];
+  __threadfence_system();
+  atomicAdd_system(ep_flags(p.peer[d]) + p.rank, 1u);
+  if (d == 0) *p.ticket = 0u;
+}
+
 // ---- permute / combine (permute.cu)
 struct PermuteParams {
   const void* x;
@@ -59,6 +168,12 @@ struct PermuteParams {
   int32_t* pos_of;               // [T, K] destination row of (t, k)
   int64_t* send_token;           // [T*K] token index of each send row (nullable)
   int64_t* send_slot;            // [T*K] top-k slot of each send row (nullable)
+  // Peer mode (permute fused with the expert-parallel dispatch): rows go straight to
+  // the owning ranks' receive regions instead of `send`; the last CTA writes every
+  // destination's metadata and raises its arrival flag.
+  int peer_mode = 0;
+  const int32_t* slot_offsets = nullptr;  // [num_slots + 1] (router output)
+  EpParams ep;
 };
 
 struct CombineParams {
@@ -73,6 +188,14 @@ struct CombineParams {
   const float* shared_gate;  // [T] or null (gate == 1)
   void* out;              // [T, H]
   int64_t ldo;
+  // Peer mode (wait_n > 0): y is this rank's combine region; wait until the G flags
+  // wait_flags[0..G) pass *wait_expect, then advance *wait_expect (last CTA, ticket).
+  const uint32_t* wait_flags = nullptr;
+  int wait_n = 0;
+  uint32_t* wait_expect = nullptr;
+  uint32_t* wait_ticket = nullptr;
+  uint64_t wait_timeout_ns = 0;
+  int* status = nullptr;
 };
 
 // ---- residual add + RMSNorm (norm.cu)
@@ -117,6 +240,7 @@ struct GemmLaunch {
   const void* w;        // [P * w_rows, K] bf16 weights (row stride K)
   GemmParams p;
   int variant = kGemmAuto;
+  int64_t rows_hint = 0;  // expected rows (kernel choice); 0: rows_cap
 };
 
 // 2D bf16 K-major TMA map (rows x cols, row stride ld elements), box box_rows x 64,
@@ -136,6 +260,13 @@ struct GemmF32Params {
   int64_t ldo;
   const int32_t* out_row_map;
 };
+
+int launch_ep_dispatch(const EpParams& p, const void* send, const int32_t* slot_offsets, int64_t max_rows,
+                       cudaStream_t stream);
+int launch_ep_collect(const EpParams& p, void* xe, int32_t* row_map, int32_t* expert_offsets,
+                      uint32_t* expect, uint64_t timeout_ns, int64_t max_rows, cudaStream_t stream);
+int launch_ep_combine_send(const EpParams& p, const void* y_recv, int64_t max_rows, cudaStream_t stream);
+int launch_ep_wait_comb(const EpParams& p, uint32_t* expect, uint64_t timeout_ns, cudaStream_t stream);
 
 int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t stream);
 int launch_grouped_gemm_f32(const GemmF32Params& p, bool swiglu, cudaStream_t stream);

@@ -10,7 +10,10 @@
 // entries stably (flat index order within a slot) with warp match/ballot and writes
 // every token row to its K destinations with 16-byte vector stores.  Rows of one
 // destination rank are contiguous ([dst rank][local slot][token order]) because
-// physical slot ids are rank-major.
+// physical slot ids are rank-major.  In peer mode (fused with the expert-parallel
+// dispatch) the K stores of a row go straight to the owning ranks' receive regions
+// over NVLink, and the last CTA publishes the counts and raises the arrival flags
+// (the protocol is described in ep_nvlink.cu).
 //
 // combine_rows mirrors the reference's unpermute
 //   out = zeros(T, H); out.index_add_(0, send_indices, y * w[send_indices, send_topk])
@@ -23,9 +26,12 @@ namespace b200moe {
 
 constexpr int PM_MAX_ENTRIES = 64 * 8;  // tb * K must not exceed this
 
-__global__ void __launch_bounds__(256) permute_rows(PermuteParams p) {
+template <bool PEER>
+__global__ void __launch_bounds__(256) permute_rows(const __grid_constant__ PermuteParams p) {
   extern __shared__ int32_t running[];     // [num_slots], -1 == not yet touched
   __shared__ int32_t pos[PM_MAX_ENTRIES];  // destination row of each entry of this block
+  __shared__ uint8_t* dst_row[PEER ? PM_MAX_ENTRIES : 1];  // peer mode: where each entry goes
+  __shared__ int s_last;
   pdl_trigger();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -63,7 +69,21 @@ __global__ void __launch_bounds__(256) permute_rows(PermuteParams p) {
     p.pos_of[flat0 + i] = d;
     if (p.send_token) p.send_token[d] = t0 + i / p.K;
     if (p.send_slot) p.send_slot[d] = i % p.K;
+    if (PEER) {
+      // send row d of slot s -> row (rank * cap + j) of the owner's receive region,
+      // j = d - (first send row of the owner rank)
+      const EpParams& ep = p.ep;
+      const int g = p.phys_ids[flat0 + i] / ep.P;
+      const int64_t j = d - p.slot_offsets[g * ep.P];
+      uint8_t* dst = nullptr;
+      if (j >= 0 && j < ep.cap_rows)
+        dst = ep_recv_rows(ep.peer[g], ep) + (static_cast<int64_t>(ep.rank) * ep.cap_rows + j) * p.row_bytes;
+      else
+        record_status(ep.status, kStatusCapacity);
+      dst_row[i] = dst;
+    }
   }
+  if (PEER) __syncthreads();
 
   // Row copies: one warp per token; the token row is read once and written K times.
   const int vec_per_row = p.row_bytes / 16;
@@ -73,19 +93,31 @@ __global__ void __launch_bounds__(256) permute_rows(PermuteParams p) {
     for (int v = lane; v < vec_per_row; v += 32) {
       const uint4 val = __ldg(src + v);
       for (int k = 0; k < p.K; ++k) {
-        const int d = pos[lt * p.K + k];
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.send) +
-                                              static_cast<int64_t>(d) * p.row_bytes);
+        uint4* dst;
+        if (PEER) {
+          uint8_t* row = dst_row[lt * p.K + k];
+          if (row == nullptr) continue;
+          dst = reinterpret_cast<uint4*>(row);
+        } else {
+          dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.send) +
+                                         static_cast<int64_t>(pos[lt * p.K + k]) * p.row_bytes);
+        }
         dst[v] = val;
       }
     }
   }
+  if (PEER) {
+    if (last_cta(p.ep.ticket, &s_last) && threadIdx.x < p.ep.G)
+      ep_publish_dispatch(p.ep, p.slot_offsets, threadIdx.x);
+  }
 }
 
-template <typename E>
+// 8 consecutive elements -> fp32.  L2_ONLY reads through L2 only (rows that another
+// GPU wrote while this kernel was running); otherwise the read-only data path.
+template <typename E, bool L2_ONLY = false>
 __device__ __forceinline__ void load8(const E* p, float (&v)[8]);
 template <>
-__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+__device__ __forceinline__ void load8<__nv_bfloat16, false>(const __nv_bfloat16* p, float (&v)[8]) {
   const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
@@ -96,9 +128,27 @@ __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, flo
   }
 }
 template <>
-__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+__device__ __forceinline__ void load8<__nv_bfloat16, true>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float, false>(const float* p, float (&v)[8]) {
   const float4 a = __ldg(reinterpret_cast<const float4*>(p));
   const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<float, true>(const float* p, float (&v)[8]) {
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldcg(reinterpret_cast<const float4*>(p) + 1);
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
@@ -121,10 +171,8 @@ __device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
 
 // One warp per (token, 256-column chunk): all K expert rows of the chunk are loaded
 // before any arithmetic, so a token's gathers are in flight together.
-template <typename E>
-__global__ void __launch_bounds__(256) combine_rows(CombineParams p) {
-  pdl_trigger();
-  pdl_wait();
+template <typename E, bool PEER>
+__device__ __forceinline__ void combine_body(const CombineParams& p) {
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int chunks = (p.H + 255) / 256;
@@ -140,7 +188,7 @@ __global__ void __launch_bounds__(256) combine_rows(CombineParams p) {
     if (k < p.K) {
       const int row = p.pos_of[static_cast<int64_t>(t) * p.K + k];
       wts[k] = p.topk_w[static_cast<int64_t>(t) * p.K + k];
-      load8<E>(y + static_cast<int64_t>(row) * p.ldy + c, v[k]);
+      load8<E, PEER>(y + static_cast<int64_t>(row) * p.ldy + c, v[k]);
     }
   }
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -161,22 +209,62 @@ __global__ void __launch_bounds__(256) combine_rows(CombineParams p) {
   store8<E>(static_cast<E*>(p.out) + static_cast<int64_t>(t) * p.ldo + c, acc);
 }
 
+// PEER: y is this rank's combine region, filled by the ranks that hold its experts.
+// Every CTA first waits (bounded) until each of them raised its flag past the count
+// this rank consumed; the last CTA to finish advances that count.
+template <typename E, bool PEER>
+__global__ void __launch_bounds__(256) combine_rows(const __grid_constant__ CombineParams p) {
+  __shared__ uint32_t s_target;
+  __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
+  if (PEER) {
+    if (threadIdx.x == 0) {
+      const uint32_t target = *p.wait_expect + 1u;
+      bool ok = true;
+      for (int d = 0; d < p.wait_n && ok; ++d) ok = wait_flag_geq(p.wait_flags + d, target, p.wait_timeout_ns, p.status);
+      if (!ok) record_status(p.status, kStatusTimeout);
+      s_target = target;
+    }
+    __syncthreads();
+  }
+  combine_body<E, PEER>(p);
+  if (PEER) {
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = (atomicAdd(p.wait_ticket, 1u) == gridDim.x - 1);
+    __syncthreads();
+    if (s_last && threadIdx.x == 0) {
+      *p.wait_expect = s_target;
+      *p.wait_ticket = 0u;
+    }
+  }
+}
+
 int launch_permute(const PermuteParams& p, cudaStream_t stream) {
-  if (p.T == 0) return 0;
   const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t);
-  launch_kernel(permute_rows, dim3(p.nblocks), dim3(256), smem, stream, p);
+  if (p.peer_mode)  // always launched: a rank without tokens still publishes empty counts
+    return launch_kernel(permute_rows<true>, dim3(p.nblocks > 0 ? p.nblocks : 1), dim3(256), smem, stream, p) ==
+                   cudaSuccess
+               ? 0
+               : -2;
+  if (p.T == 0) return 0;
+  launch_kernel(permute_rows<false>, dim3(p.nblocks), dim3(256), smem, stream, p);
   return 0;
 }
 
 int launch_combine(const CombineParams& p, cudaStream_t stream) {
-  if (p.T == 0) return 0;
+  const bool peer = p.wait_n > 0;
+  if (p.T == 0 && !peer) return 0;  // peer mode always runs: it consumes the arrival flags
   const int64_t warps = static_cast<int64_t>(p.T) * ((p.H + 255) / 256);
-  const int grid = static_cast<int>((warps * 32 + 255) / 256);
+  const int grid = static_cast<int>(max64(1, (warps * 32 + 255) / 256));
+  cudaError_t e;
   if (p.dtype == kDtypeBF16)
-    launch_kernel(combine_rows<__nv_bfloat16>, dim3(grid), dim3(256), 0, stream, p);
+    e = peer ? launch_kernel(combine_rows<__nv_bfloat16, true>, dim3(grid), dim3(256), 0, stream, p)
+             : launch_kernel(combine_rows<__nv_bfloat16, false>, dim3(grid), dim3(256), 0, stream, p);
   else
-    launch_kernel(combine_rows<float>, dim3(grid), dim3(256), 0, stream, p);
-  return 0;
+    e = peer ? launch_kernel(combine_rows<float, true>, dim3(grid), dim3(256), 0, stream, p)
+             : launch_kernel(combine_rows<float, false>, dim3(grid), dim3(256), 0, stream, p);
+  return e == cudaSuccess ? 0 : -2;
 }
 
 }  // namespace b200moe

@@ -12,12 +12,16 @@ easyinfra/generation/blocks/moe/moe_all2all.py):
 
 With one rank (G == 1) the whole layer runs without a host synchronisation: the
 router's last CTA writes the per-expert row offsets the grouped GEMMs read.  With
-G > 1 the layer synchronises once, after the count all-gather, exactly where the
-reference does (moe_all2all.py:410-424), because NCCL's all_to_all_single takes host
-split lists.  The received rows ([source rank][local slot] order) are regrouped into
-expert-major order by one gather kernel that also records the inverse row map; the
-down GEMM scatters its output rows straight back to received order, ready for the
-combine all-to-all.
+G > 1 there are two transports:
+  * "nvlink" (a PeerExchange): the rows move through peer memory with four kernels
+    and device-side flags (peer_exchange.py) — no host synchronisation, so a stack of
+    layers captures into one CUDA graph per rank;
+  * NCCL (a GroupCommunicator only): the layer synchronises once, after the count
+    all-gather, exactly where the reference does (moe_all2all.py:410-424), because
+    all_to_all_single takes host split lists.  The received rows ([source rank][local
+    slot] order) are regrouped expert-major by one gather kernel that also records the
+    inverse row map; the down GEMM scatters its rows straight back to received order,
+    ready for the combine all-to-all.
 """
 from __future__ import annotations
 
@@ -98,8 +102,9 @@ class MoELayer:
                  rank: int = 0, comm: Optional[GroupCommunicator] = None,
                  routed_scaling_factor: float = 1.0, shared_gate: bool = False,
                  status: Optional[torch.Tensor] = None, scoring: str = "softmax",
-                 n_group: int = 1, topk_group: int = 1):
+                 n_group: int = 1, topk_group: int = 1, exchange=None):
         self.p = params
+        self.exchange = exchange  # PeerExchange: the NVLink transport for G > 1
         self.placement = placement
         self.top_k = top_k
         self.norm_topk_prob = norm_topk_prob
@@ -227,9 +232,37 @@ class MoELayer:
                                      residual_out=residual_out, normed=nbuf)
         return ro, self.forward(normed, out=out)
 
+    # ------------------------------------------------------------ NVLink transport
+    def peer_dispatch(self, st: DispatchState) -> None:
+        self.exchange.dispatch(st.perm.send, st.route.slot_offsets, st.T * self.top_k)
+
+    def peer_experts(self, st: DispatchState) -> None:
+        """Collect the rows of every source, run both GEMMs (the down GEMM writes back
+        into the receive region, in arrival order) and send the rows home."""
+        xg = self.exchange
+        hint = st.T * self.top_k
+        xe, row_map, offs = xg.collect(rows_hint=hint)
+        act = ops.grouped_swiglu(xe, offs, self.p.w_gate_up, out=xg.act, status=self.status, rows_hint=hint)
+        y = ops.grouped_down(act, offs, self.p.w_down, out=xg.recv, out_row_map=row_map,
+                             status=self.status, rows_hint=hint)
+        xg.combine_send(y, rows_hint=hint)
+
+    def peer_finish(self, st: DispatchState, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        back = self.exchange.wait_combine(st.T * self.top_k)
+        return self.unpermute(st, back, out)
+
+    def forward_peer(self, x: torch.Tensor, st: DispatchState,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        self.peer_dispatch(st)
+        self.shared_expert(x, st)  # overlaps the other ranks' rows arriving
+        self.peer_experts(st)
+        return self.peer_finish(st, out)
+
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Routed output plus the (gated) shared-expert output for this rank's tokens."""
         st = self.route_and_permute(x)
+        if self.G > 1 and self.exchange is not None:
+            return self.forward_peer(x, st, out)
         self.shared_expert(x, st)
         if self.G == 1:
             y = self.experts_local(st)
@@ -270,3 +303,17 @@ def forward_ep_single_device(layers: List[MoELayer], xs: List[torch.Tensor],
             parts.append(ys[d][a:a + sts[d].recv_splits[r]])
         outs.append(l.unpermute(st, torch.cat(parts, 0)))
     return (outs, sts) if return_states else outs
+
+
+def forward_peer_single_device(layers: List[MoELayer], xs: List[torch.Tensor]) -> List[torch.Tensor]:
+    """The NVLink transport with all G ranks in one process on one device: every layer
+    carries a PeerExchange from PeerExchange.local_group, and each stage runs for all
+    ranks before the next one starts, so every flag a kernel checks is already set."""
+    sts = [l.route_and_permute(x) for l, x in zip(layers, xs)]
+    for l, st in zip(layers, sts):
+        l.peer_dispatch(st)
+    for l, x, st in zip(layers, xs, sts):
+        l.shared_expert(x, st)
+    for l, st in zip(layers, sts):
+        l.peer_experts(st)
+    return [l.peer_finish(st) for l, st in zip(layers, sts)]

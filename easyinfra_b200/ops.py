@@ -247,8 +247,9 @@ def permute(x: torch.Tensor, r: RouterOutput, *, num_slots: int, E1: int,
 
 def grouped_swiglu(x: torch.Tensor, expert_offsets: torch.Tensor, w_gate_up: torch.Tensor,
                    *, out: Optional[torch.Tensor] = None,
-                   status: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """act = silu(x Wg^T) * (x Wu^T) per expert segment; x [rows, H] bf16 expert-major."""
+                   status: Optional[torch.Tensor] = None, rows_hint: int = 0) -> torch.Tensor:
+    """act = silu(x Wg^T) * (x Wu^T) per expert segment; x [rows, H] bf16 expert-major.
+    rows_hint: expected rows when x is a worst-case buffer (picks the kernel)."""
     _need_cuda(x, expert_offsets, w_gate_up, status)
     if x.dtype != w_gate_up.dtype or x.dtype not in (torch.bfloat16, torch.float32):
         raise TypeError("grouped GEMMs take bfloat16 (tensor cores) or float32 activations and weights")
@@ -266,9 +267,9 @@ def grouped_swiglu(x: torch.Tensor, expert_offsets: torch.Tensor, w_gate_up: tor
         _count(1 if x.shape[0] else 0)
         return act
     _hook("grouped_swiglu", "start")
-    _lib.call("b200moe_grouped_swiglu", x.data_ptr(), x.stride(0), x.shape[0], offs.data_ptr(),
-              P, H, I, w_gate_up.data_ptr(), act.data_ptr(), act.stride(0), _ptr(status),
-              _stream())
+    _lib.call("b200moe_grouped_swiglu_ex", x.data_ptr(), x.stride(0), x.shape[0], rows_hint,
+              offs.data_ptr(), P, H, I, w_gate_up.data_ptr(), act.data_ptr(), act.stride(0),
+              _ptr(status), _stream())
     _hook("grouped_swiglu", "end")
     _count(1 if x.shape[0] else 0)
     return act
@@ -277,8 +278,9 @@ def grouped_swiglu(x: torch.Tensor, expert_offsets: torch.Tensor, w_gate_up: tor
 def grouped_down(act: torch.Tensor, expert_offsets: torch.Tensor, w_down: torch.Tensor, *,
                  out: Optional[torch.Tensor] = None,
                  out_row_map: Optional[torch.Tensor] = None,
-                 status: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y = act Wd^T per expert segment (optionally scattering rows through out_row_map)."""
+                 status: Optional[torch.Tensor] = None, rows_hint: int = 0) -> torch.Tensor:
+    """y = act Wd^T per expert segment (optionally scattering rows through out_row_map).
+    rows_hint: expected rows when act is a worst-case buffer (picks the kernel)."""
     _need_cuda(act, expert_offsets, w_down, out_row_map, status)
     if act.dtype != w_down.dtype or act.dtype not in (torch.bfloat16, torch.float32):
         raise TypeError("grouped GEMMs take bfloat16 (tensor cores) or float32 activations and weights")
@@ -296,7 +298,7 @@ def grouped_down(act: torch.Tensor, expert_offsets: torch.Tensor, w_down: torch.
         _count(1 if act.shape[0] else 0)
         return y
     _hook("grouped_down", "start")
-    _lib.call("b200moe_grouped_down", act.data_ptr(), act.stride(0), act.shape[0],
+    _lib.call("b200moe_grouped_down_ex", act.data_ptr(), act.stride(0), act.shape[0], rows_hint,
               offs.data_ptr(), P, H, I, w_down.data_ptr(), y.data_ptr(), y.stride(0),
               _ptr(out_row_map), _ptr(status), _stream())
     _hook("grouped_down", "end")

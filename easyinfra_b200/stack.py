@@ -4,8 +4,11 @@ With one rank (G == 1) a layer forward never synchronises with the host: the rou
 last CTA writes the expert row offsets that the grouped GEMMs read, so a whole stack
 of layers can be recorded once as a CUDA graph and replayed per batch.  That removes
 the per-launch host cost (8 C-ABI launches per layer) that dominates small decode
-batches.  Expert-parallel stacks (G > 1) run eagerly: their count exchange needs a
-host round trip before NCCL's all-to-all.
+batches.  Expert-parallel stacks (G > 1) capture the same way when their layers use
+the NVLink transport (a PeerExchange: flags on the device, no host round trip); every
+rank then captures and replays its own graph, the same number of times.  With the
+NCCL transport they run eagerly: the count exchange needs a host round trip before
+all_to_all_single.
 """
 from __future__ import annotations
 
@@ -44,9 +47,11 @@ class MoEStack:
 
     def capture(self, tokens: int, warmup: int = 2,
                 on_capture: Optional[Callable[[], None]] = None) -> "CapturedStack":
-        """Record forward() for `tokens` tokens into a CUDA graph (G == 1 only)."""
-        if any(l.G != 1 for l in self.layers):
-            raise ValueError("only single-rank stacks can be captured (EP needs a host sync)")
+        """Record forward() for `tokens` tokens into a CUDA graph (G == 1, or G > 1 over
+        the NVLink transport; collective: every rank of the group calls it)."""
+        if any(l.G != 1 and l.exchange is None for l in self.layers):
+            raise ValueError("expert-parallel stacks capture only over the NVLink transport "
+                             "(the NCCL path needs a host sync)")
         lay0 = self.layers[0]
         x = torch.zeros(tokens, lay0.H, dtype=lay0.p.gate_w.dtype, device=lay0.device)
         side = torch.cuda.Stream(device=lay0.device)

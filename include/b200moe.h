@@ -5,7 +5,8 @@
  * all-to-all MoE block as plain C entry points: device pointers, sizes and a CUDA
  * stream, no framework types.  Host code (the Python package easyinfra_b200, or a
  * ctypes stub inside EasyInfra itself) owns every buffer; no entry point allocates
- * device memory.  Every call is asynchronous on the given stream and returns 0 on
+ * device memory except b200moe_ep_alloc, which creates the peer-mapped exchange
+ * buffer of the expert-parallel path.  Every call is asynchronous on the given stream and returns 0 on
  * success or a negative B200MOE_E* code; b200moe_last_error() describes the last
  * failure of the calling thread.  Conditions that only the device can see (an
  * out-of-range index, a bounded wait that timed out) are recorded in an optional
@@ -253,6 +254,87 @@ B200MOE_API int b200moe_gather_segments(const void* src, void* dst, int64_t row_
                             const int32_t* src_start, const int32_t* dst_start,
                             const int32_t* len, int nseg, int64_t max_rows,
                             int32_t* dst_to_src, void* stream);
+
+/*
+ * Grouped GEMMs with a row-count hint: as b200moe_grouped_swiglu / b200moe_grouped_down,
+ * but the kernel (weight-major for decode, token-major for prefill) is chosen from
+ * rows_hint, the expected row count, instead of rows_cap.  For callers whose
+ * activation buffer is sized for the worst case while the rows live on the device
+ * (the peer exchange below).  rows_hint 0 behaves like the plain entry points.
+ * No counterpart in the reference (its all-to-all path knows the row count on the host).
+ */
+B200MOE_API int b200moe_grouped_swiglu_ex(const void* x, int64_t ldx, int64_t rows_cap, int64_t rows_hint,
+                                          const int32_t* expert_offsets, int P, int H, int I,
+                                          const void* w_gate_up, void* act, int64_t ld_act, int* status,
+                                          void* stream);
+B200MOE_API int b200moe_grouped_down_ex(const void* act, int64_t ld_act, int64_t rows_cap, int64_t rows_hint,
+                                        const int32_t* expert_offsets, int P, int H, int I,
+                                        const void* w_down, void* out, int64_t ldo,
+                                        const int32_t* out_row_map, int* status, void* stream);
+
+/*
+ * Expert-parallel token exchange over NVLink peer memory (one process per GPU).
+ *
+ * Replaces the count all-gather, the host synchronisation and the two NCCL
+ * all_to_all_single calls of MoeAll2AllBlock (easyinfra/generation/blocks/moe/
+ * moe_all2all.py:397-444 dispatch, :560-591 combine; GroupCommunicator.all_to_all_single,
+ * easyinfra/generation/parallel/communicator.py:269) with four stream-ordered launches that need
+ * no host round trip and can be captured in a CUDA graph:
+ *   b200moe_ep_dispatch      send rows (router send order, rank-major slots) -> the
+ *                            owning ranks' buffers, then raise their arrival flags;
+ *   b200moe_ep_collect       wait for every rank's rows, regroup them expert-major
+ *                            (x for the grouped GEMMs), write expert_offsets [P+1] and
+ *                            row_map (the down GEMM's out_row_map);
+ *   b200moe_ep_combine_send  down-GEMM rows (arrival order, y_recv) -> the sources'
+ *                            combine regions at their send positions, raise flags;
+ *   b200moe_ep_wait_combine  wait until every rank returned this rank's rows; the
+ *                            combine region (b200moe_ep_layout comb_offset) then holds
+ *                            the expert outputs in send order for b200moe_combine.
+ * Each rank creates one buffer with b200moe_ep_alloc, exchanges the 64-byte handles
+ * (any host collective), maps every peer's with b200moe_ep_open and fills a
+ * b200moe_ep_desc.  counters (8 x uint32, device, zeroed once) hold the kernels'
+ * tickets and how many arrivals this rank consumed; every rank must issue the four
+ * calls in the same order.  Every wait is bounded by timeout_ns; on timeout the
+ * status word gets B200MOE_STATUS_TIMEOUT and the kernel proceeds with what arrived
+ * (the caller must treat the layer output as invalid).  timeout_ns == 0 checks each
+ * flag once without waiting: for running all ranks' launches in stream order on a
+ * single device.
+ */
+#define B200MOE_EP_MAX_RANKS 8
+#define B200MOE_EP_HANDLE_BYTES 64
+
+typedef struct b200moe_ep_desc {
+  void* peer[B200MOE_EP_MAX_RANKS]; /* every rank's exchange buffer, as mapped in this process */
+  int world_size;                   /* G <= B200MOE_EP_MAX_RANKS */
+  int rank;
+  int slots_per_rank;               /* P */
+  int row_bytes;                    /* H * element bytes, multiple of 16 */
+  int64_t cap_rows;                 /* rows one source may send to one rank */
+  int64_t comb_rows;                /* rows this rank sends per layer at most (T * K) */
+  uint32_t* counters;               /* device, 8 x uint32, zero before the first call */
+  int* status;                      /* device status word (nullable) */
+  uint64_t timeout_ns;
+} b200moe_ep_desc;
+
+/* Byte offsets inside every rank's exchange buffer and its total size. */
+B200MOE_API int b200moe_ep_layout(int world_size, int slots_per_rank, int64_t cap_rows, int64_t comb_rows,
+                                  int row_bytes, int64_t* recv_offset, int64_t* comb_offset,
+                                  int64_t* total_bytes);
+/* Allocate and zero this rank's exchange buffer on the current device; writes its
+ * inter-process handle (B200MOE_EP_HANDLE_BYTES). */
+B200MOE_API int b200moe_ep_alloc(size_t bytes, void** buffer, void* handle);
+/* Map a peer's buffer from its handle (enables peer access on first use). */
+B200MOE_API int b200moe_ep_open(const void* handle, void** peer_buffer);
+B200MOE_API int b200moe_ep_close(void* peer_buffer);
+B200MOE_API int b200moe_ep_free(void* buffer);
+
+B200MOE_API int b200moe_ep_dispatch(const b200moe_ep_desc* ep, const void* send, const int32_t* slot_offsets,
+                                    int64_t send_rows, void* stream);
+B200MOE_API int b200moe_ep_collect(const b200moe_ep_desc* ep, void* x_expert, int32_t* row_map,
+                                   int32_t* expert_offsets, int64_t rows_hint, void* stream);
+B200MOE_API int b200moe_ep_combine_send(const b200moe_ep_desc* ep, const void* y_recv, int64_t rows_hint,
+                                        void* stream);
+B200MOE_API int b200moe_ep_wait_combine(const b200moe_ep_desc* ep, void* stream);
 
 #ifdef __cplusplus
 }

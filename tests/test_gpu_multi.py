@@ -1,7 +1,10 @@
-"""Expert-parallel MoE layer across real GPUs with NCCL (marked gpu; skipped with fewer
-than 2 GPUs).  Each rank runs MoELayer.forward with its own tokens and slots; the
-count all-gather and both all-to-alls go through NCCL; every rank's output is
-checked against the CPU oracle's simulation of the same EP layer."""
+"""Expert-parallel MoE layer across real GPUs (marked gpu; skipped with fewer than 2
+GPUs).  Each rank runs MoELayer.forward with its own tokens and slots, over either
+transport: NCCL (count all-gather, host sync, two all_to_all_single) or NVLink peer
+memory (PeerExchange: four kernels, device flags, no host sync).  Every rank's output
+is checked against the CPU oracle's simulation of the same EP layer; the NVLink
+transport must also give the NCCL transport's output bit for bit, and a two-layer
+stack captured in a CUDA graph per rank must replay to its eager output."""
 from __future__ import annotations
 
 import datetime
@@ -24,7 +27,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, case_name, q):
+def _worker(rank, world, port, case_name, transport, q):
     import torch.distributed as dist
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -59,9 +62,20 @@ def _worker(rank, world, port, case_name, q):
                        shared_gate=shape.shared_gate)
         T = case["T"]
         xs = [C.hidden_states(shape, T, rank=r) for r in range(world)]
+        xg = None
+        same_as_nccl = True
+        if transport == "nvlink":
+            from easyinfra_b200.peer_exchange import PeerExchange
+            out_nccl = lay.forward(xs[rank].to(dev))
+            xg = PeerExchange.create(comm, rank=rank, world_size=world, slots_per_rank=P, hidden=lay.H,
+                                     inter=lay.I, dtype=shape.dtype, max_tokens=T, top_k=shape.top_k,
+                                     device=dev, timeout_s=5.0)
+            lay.exchange = xg
         out = lay.forward(xs[rank].to(dev))
         out2 = lay.forward(xs[rank].to(dev))     # second call: buffers and tables reused
         torch.cuda.synchronize()
+        if xg is not None:
+            same_as_nccl = bool(torch.equal(out, out_nccl))
         st = lay.route_and_permute(xs[rank].to(dev))
         ids = st.route.topk_ids.cpu().long()
         lw = O.LayerWeights(gw[:shape.num_experts], wgu_all, wd_all,
@@ -72,7 +86,22 @@ def _worker(rank, world, port, case_name, q):
         same = (ids == ref[rank].ids).all(-1)
         exp = O.layer_output(ref[rank]).float()[same]
         err = float((out.cpu().float()[same] - exp).abs().max() / exp.abs().max())
-        rep = bool(torch.equal(out, out2))
+        rep = bool(torch.equal(out, out2)) and same_as_nccl
+        if xg is not None:
+            # two chained layers captured in one CUDA graph per rank vs eager
+            from easyinfra_b200.stack import MoEStack
+            lay2 = MoELayer(params, pl, shape.top_k, shape.norm_topk_prob, rank=rank, comm=comm,
+                            shared_gate=shape.shared_gate, exchange=xg)
+            stack = MoEStack([lay, lay2])
+            x = xs[rank].to(dev)
+            eager = stack.forward(x).clone()
+            cap = stack.capture(T)
+            g1 = cap(x).clone()
+            g2 = cap(x).clone()
+            torch.cuda.synchronize()
+            rep = rep and bool(torch.equal(g1, eager)) and bool(torch.equal(g2, eager))
+            del cap
+            xg.close(comm)
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
         q.put((rank, err, int((~same).sum()), rep, None))
@@ -80,15 +109,17 @@ def _worker(rank, world, port, case_name, q):
         q.put((rank, None, None, None, traceback.format_exc()))
 
 
+@pytest.mark.parametrize("transport", ["nccl", "nvlink"])
 @pytest.mark.parametrize("case_name", ["mixtral_g2", "qwen3_g8", "dsv2_g2"])
-def test_ep_layer_over_nccl(case_name):
+def test_ep_layer_multi_gpu(case_name, transport):
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, case_name, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case_name, transport, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=600) for _ in procs]
@@ -97,5 +128,5 @@ def test_ep_layer_over_nccl(case_name):
     for rank, err, excluded, rep, tb in res:
         assert tb is None, f"rank {rank}:\n{tb}"
         assert err < 6e-3, (rank, err)
-        assert rep, "two calls of the same layer gave different outputs"
+        assert rep, "repeated calls, transports or graph replays gave different outputs"
         assert excluded <= 2
