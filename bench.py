@@ -60,9 +60,10 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (invalid as a result)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--transport", default="nvlink", choices=["nvlink", "nccl"],
-                    help="expert-parallel row exchange for --gpus > 1: peer memory (graph-captured) "
-                         "or NCCL all_to_all_single (the reference's, host sync per layer)")
+    ap.add_argument("--transport", default="nvlink", choices=["nvlink", "nvlink_plain", "nccl"],
+                    help="expert-parallel row exchange for --gpus > 1: peer memory with the fused "
+                         "kernels (graph-captured), peer memory with separate exchange kernels, or "
+                         "NCCL all_to_all_single (the reference's, host sync per layer)")
     return ap.parse_args()
 
 
@@ -233,14 +234,15 @@ def run_ours(args):
     hbm, bf16_burst, bf16_sus, peak_kind = peaks()
     xg = None
     xg_status = torch.zeros(1, dtype=torch.int32, device=device)
-    if world > 1 and args.transport == "nvlink":
+    if world > 1 and args.transport.startswith("nvlink"):
         from easyinfra_b200.peer_exchange import PeerExchange
         wls = [args.workload] + ([] if args.no_secondary else SECONDARY.get(args.workload, []))
         max_t = max(WORKLOADS[w][2] for w in wls if WORKLOADS[w][0] == cfg_key)
         lay0 = layers[0]
         xg = PeerExchange.create(group, rank=rank, world_size=world, slots_per_rank=lay0.P, hidden=lay0.H,
                                  inter=lay0.I, dtype=shape.dtype, max_tokens=max_t, top_k=shape.top_k,
-                                 device=device, timeout_s=10.0, status=xg_status)
+                                 device=device, timeout_s=10.0, status=xg_status,
+                                 fused=args.transport == "nvlink")
         for lay in layers:
             lay.exchange = xg
     use_graph = world == 1 or xg is not None

@@ -110,9 +110,21 @@ SIGNATURES = {
     "b200moe_ep_close": (c_int, [c_void_p]),
     "b200moe_ep_free": (c_int, [c_void_p]),
     "b200moe_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
-    "b200moe_ep_collect": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "b200moe_ep_collect": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "b200moe_ep_combine_send": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "b200moe_ep_wait_combine": (c_int, [c_void_p, c_void_p]),
+    "b200moe_ep_permute_dispatch": (
+        c_int,
+        [c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_size_t, c_void_p]),
+    "b200moe_ep_grouped_down_send": (
+        c_int,
+        [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
+         c_void_p, c_void_p]),
+    "b200moe_ep_combine": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p,
+         c_int64, c_void_p]),
 }
 
 EP_MAX_RANKS = 8

@@ -572,8 +572,10 @@ int b200moe_gather_segments(const void* src, void* dst, int64_t row_bytes,
 }
 
 // ------------------------------------------------------------------ peer exchange
-// counters[0..2]: tickets of dispatch / collect / combine_send; counters[3]: dispatch
-// arrivals consumed; counters[4]: combine arrivals consumed.
+// counters[0..2]: tickets of dispatch (or permute-dispatch) / collect / combine_send;
+// counters[3]: dispatch arrivals consumed; counters[4]: combine arrivals consumed;
+// counters[5]: ticket of the combine that waits itself; counters[6]: ticket of the down
+// GEMM that sends its rows.
 static_assert(sizeof(cudaIpcMemHandle_t) == B200MOE_EP_HANDLE_BYTES, "IPC handle size");
 
 }  // extern "C"
@@ -686,18 +688,21 @@ int b200moe_ep_dispatch(const b200moe_ep_desc* ep, const void* send, const int32
   return check_launch("ep_dispatch");
 }
 
-int b200moe_ep_collect(const b200moe_ep_desc* ep, void* x_expert, int32_t* row_map, int32_t* expert_offsets,
-                       int64_t rows_hint, void* stream) {
+int b200moe_ep_collect(const b200moe_ep_desc* ep, void* x_expert, int32_t* row_map, int32_t* peer_row_map,
+                       int32_t* expert_offsets, int64_t rows_hint, void* stream) {
   int rc;
   if ((rc = device_ok())) return rc;
   EpParams p;
   if ((rc = ep_params(ep, &p))) return rc;
-  if (x_expert == nullptr || !aligned16(x_expert) || row_map == nullptr || expert_offsets == nullptr)
+  if (x_expert == nullptr || !aligned16(x_expert) || (row_map == nullptr && peer_row_map == nullptr) ||
+      expert_offsets == nullptr)
     return fail(B200MOE_EINVAL, "collect: null or misaligned output");
+  if (peer_row_map != nullptr && ep->comb_rows > (int64_t(1) << kPeerRowBits))
+    return fail(B200MOE_EUNSUPPORTED, "peer row map holds at most 2^%d rows per rank", kPeerRowBits);
   p.ticket = ep->counters + 1;
   const int64_t rows = rows_hint > 0 ? rows_hint : static_cast<int64_t>(p.G) * p.cap_rows;
-  if (launch_ep_collect(p, x_expert, row_map, expert_offsets, ep->counters + 3, ep->timeout_ns, rows,
-                        static_cast<cudaStream_t>(stream)))
+  if (launch_ep_collect(p, x_expert, row_map, peer_row_map, expert_offsets, ep->counters + 3, ep->timeout_ns,
+                        rows, static_cast<cudaStream_t>(stream)))
     return fail(B200MOE_ECUDA, "ep_collect launch: %s", cudaGetErrorString(cudaGetLastError()));
   return check_launch("ep_collect");
 }
@@ -713,6 +718,142 @@ int b200moe_ep_combine_send(const b200moe_ep_desc* ep, const void* y_recv, int64
   if (launch_ep_combine_send(p, y_recv, rows, static_cast<cudaStream_t>(stream)))
     return fail(B200MOE_ECUDA, "ep_combine_send launch: %s", cudaGetErrorString(cudaGetLastError()));
   return check_launch("ep_combine_send");
+}
+
+int b200moe_ep_permute_dispatch(const b200moe_ep_desc* ep, const void* x, int64_t ldx, int x_dtype, int T, int H,
+                                int K, int E1, const int32_t* phys_ids, const int32_t* slot_offsets,
+                                int32_t* pos_of, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams e;
+  if ((rc = ep_params(ep, &e))) return rc;
+  if (x_dtype != B200MOE_DTYPE_BF16 && x_dtype != B200MOE_DTYPE_F32)
+    return fail(B200MOE_EUNSUPPORTED, "x_dtype=%d", x_dtype);
+  if (T < 0 || K < 1 || K > 8 || H <= 0) return fail(B200MOE_EINVAL, "T=%d K=%d H=%d", T, K, H);
+  const int row_bytes = H * dtype_bytes(x_dtype);
+  if (row_bytes != ep->row_bytes) return fail(B200MOE_EINVAL, "row bytes %d != exchange row bytes %d", row_bytes,
+                                              ep->row_bytes);
+  if (static_cast<int64_t>(T) * K > ep->comb_rows)
+    return fail(B200MOE_EINVAL, "T*K=%lld exceeds comb_rows=%lld", static_cast<long long>(T) * K,
+                static_cast<long long>(ep->comb_rows));
+  if (!slot_offsets || !workspace || (T > 0 && (!x || !phys_ids || !pos_of)))
+    return fail(B200MOE_EINVAL, "null pointer");
+  if (T > 0 && (!aligned16(x) || (ldx * dtype_bytes(x_dtype)) % 16 != 0))
+    return fail(B200MOE_EINVAL, "x must be 16-byte aligned with a 16-byte row stride");
+  if (tokens_per_block(T) * K > 512) return fail(B200MOE_EUNSUPPORTED, "tokens per block * K > 512");
+  const int num_slots = ep->world_size * ep->slots_per_rank;
+  const RouterWs ws = router_ws_layout(workspace, T, E1, num_slots);
+  if (workspace_bytes < ws.bytes)
+    return fail(B200MOE_EINVAL, "workspace too small: %zu < %zu", workspace_bytes, ws.bytes);
+  PermuteParams p;
+  p.x = x;
+  p.x_stride = ldx * dtype_bytes(x_dtype);
+  p.row_bytes = row_bytes;
+  p.T = T;
+  p.K = K;
+  p.phys_ids = phys_ids;
+  p.block_offsets = ws.block_counts;
+  p.num_slots = num_slots;
+  p.nblocks = nblocks_for(T);
+  p.tb = tokens_per_block(T);
+  p.send = nullptr;
+  p.pos_of = pos_of;
+  p.send_token = nullptr;
+  p.send_slot = nullptr;
+  p.peer_mode = 1;
+  p.slot_offsets = slot_offsets;
+  p.ep = e;
+  p.ep.ticket = ep->counters + 0;
+  if (launch_permute(p, static_cast<cudaStream_t>(stream)))
+    return fail(B200MOE_ECUDA, "ep_permute_dispatch launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("ep_permute_dispatch");
+}
+
+int b200moe_ep_grouped_down_send(const b200moe_ep_desc* ep, const void* act, int64_t ld_act, int64_t rows_cap,
+                                 int64_t rows_hint, const int32_t* expert_offsets, int P, int H, int I,
+                                 const void* w_down, const int32_t* peer_row_map, int* status, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams e;
+  if ((rc = ep_params(ep, &e))) return rc;
+  if (P != ep->slots_per_rank || H <= 0 || I <= 0 || rows_cap <= 0)
+    return fail(B200MOE_EINVAL, "P=%d H=%d I=%d rows_cap=%lld", P, H, I, static_cast<long long>(rows_cap));
+  if (H * 2 != ep->row_bytes) return fail(B200MOE_EINVAL, "bf16 rows of H=%d do not match the exchange", H);
+  if (!act || !expert_offsets || !w_down || !peer_row_map) return fail(B200MOE_EINVAL, "null pointer");
+  if (H % 32 != 0 || I % 64 != 0)
+    return fail(B200MOE_EUNSUPPORTED, "grouped_down needs H %% 32 == 0 and I %% 64 == 0 (H=%d I=%d)", H, I);
+  if (ld_act < I || ld_act % 8 != 0 || !aligned16(act) || !aligned16(w_down))
+    return fail(B200MOE_EINVAL, "bad leading dimension or alignment");
+  GemmLaunch L;
+  L.a = act;
+  L.rows_cap = rows_cap;
+  L.lda = ld_act;
+  L.w = w_down;
+  L.p.expert_offsets = expert_offsets;
+  L.p.P = P;
+  L.p.N = H;
+  L.p.K = I;
+  L.p.w_rows = H;
+  L.p.up_row = 0;
+  L.p.out = nullptr;
+  L.p.ldo = H;
+  L.p.out_row_map = peer_row_map;
+  L.p.status = status;
+  L.p.peer_out = 1;
+  for (int g = 0; g < EP_MAX_RANKS; ++g) {
+    L.p.po.base[g] = g < e.G ? e.peer[g] : nullptr;
+    L.p.po.rows[g] = g < e.G ? e.peer[g] + ep_comb_offset(e.G, e.P, e.cap_rows, e.row_bytes) : nullptr;
+  }
+  L.p.po.G = e.G;
+  L.p.po.rank = e.rank;
+  L.p.po.ticket = ep->counters + 6;
+  L.variant = gemm_variant_from_env();
+  L.rows_hint = rows_hint < 0 ? 0 : rows_hint;
+  rc = launch_grouped_down(L, static_cast<cudaStream_t>(stream));
+  if (rc == -4) return fail(B200MOE_EUNSUPPORTED, "P=%d exceeds the kernel's slot limit", P);
+  if (rc == -1) return fail(B200MOE_ECUDA, "cuTensorMapEncodeTiled failed (down)");
+  if (rc) return fail(B200MOE_ECUDA, "ep_grouped_down_send launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("ep_grouped_down_send");
+}
+
+int b200moe_ep_combine(const b200moe_ep_desc* ep, const int32_t* pos_of, const float* topk_w, int T, int K,
+                       int H, int dtype, const void* shared, int64_t lds, const float* shared_gate, void* out,
+                       int64_t ldo, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams e;
+  if ((rc = ep_params(ep, &e))) return rc;
+  if (dtype != B200MOE_DTYPE_BF16 && dtype != B200MOE_DTYPE_F32)
+    return fail(B200MOE_EUNSUPPORTED, "dtype=%d", dtype);
+  if (T < 0 || K < 1 || K > 8 || H <= 0 || H % 8 != 0) return fail(B200MOE_EINVAL, "T=%d K=%d H=%d", T, K, H);
+  const int eb = dtype_bytes(dtype);
+  if (H * eb != ep->row_bytes) return fail(B200MOE_EINVAL, "rows of H=%d do not match the exchange", H);
+  if (T > 0 && (!pos_of || !topk_w || !out)) return fail(B200MOE_EINVAL, "null pointer");
+  if ((T > 0 && !aligned16(out)) || (ldo * eb) % 16 || (shared && (!aligned16(shared) || (lds * eb) % 16)))
+    return fail(B200MOE_EINVAL, "out/shared must be 16-byte aligned with 16-byte row strides");
+  CombineParams p;
+  p.y = e.peer[e.rank] + ep_comb_offset(e.G, e.P, e.cap_rows, e.row_bytes);
+  p.ldy = H;
+  p.dtype = dtype;
+  p.pos_of = pos_of;
+  p.topk_w = topk_w;
+  p.T = T;
+  p.K = K;
+  p.H = H;
+  p.shared = shared;
+  p.lds = lds;
+  p.shared_gate = shared_gate;
+  p.out = out;
+  p.ldo = ldo;
+  p.wait_flags = reinterpret_cast<const uint32_t*>(e.peer[e.rank]) + e.G;
+  p.wait_n = e.G;
+  p.wait_expect = ep->counters + 4;
+  p.wait_ticket = ep->counters + 5;
+  p.wait_timeout_ns = ep->timeout_ns;
+  p.status = ep->status;
+  if (launch_combine(p, static_cast<cudaStream_t>(stream)))
+    return fail(B200MOE_ECUDA, "ep_combine launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch("ep_combine");
 }
 
 int b200moe_ep_wait_combine(const b200moe_ep_desc* ep, void* stream) {

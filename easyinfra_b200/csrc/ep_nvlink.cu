@@ -65,11 +65,12 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
 // ------------------------------------------------------------------ collect
 // Dynamic shared memory: cnt[G*P], base[G*P], srow[G+1], eoff[P+1] (int32).
 __global__ void __launch_bounds__(256) ep_collect_kernel(const __grid_constant__ EpParams p, uint8_t* xe, int32_t* row_map,
-                                                         int32_t* expert_offsets, uint32_t* expect,
-                                                         uint64_t timeout_ns) {
+                                                         int32_t* peer_row_map, int32_t* expert_offsets,
+                                                         uint32_t* expect, uint64_t timeout_ns) {
   extern __shared__ int32_t sm[];
   __shared__ int s_last;
   __shared__ uint32_t s_target;
+  __shared__ int s_dst[EP_MAX_RANKS];  // first combine row at each source (peer_row_map)
   pdl_trigger();
   pdl_wait();
   const int G = p.G, P = p.P;
@@ -96,6 +97,12 @@ __global__ void __launch_bounds__(256) ep_collect_kernel(const __grid_constant__
       cnt[s * P + q] = c;
       run += c;
     }
+    int dst = meta[P];
+    if (dst < 0 || static_cast<int64_t>(dst) + run > p.comb_rows) {
+      if (peer_row_map != nullptr) record_status(p.status, kStatusBadIndex);
+      dst = 0;  // keeps every store in bounds; the status word reports the fault
+    }
+    s_dst[s] = dst;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -132,7 +139,13 @@ __global__ void __launch_bounds__(256) ep_collect_kernel(const __grid_constant__
     const int64_t src = static_cast<int64_t>(s) * p.cap_rows + j;
     copy_row<true>(xe + static_cast<int64_t>(dst) * p.row_bytes, ep_recv_rows(mine, p) + src * p.row_bytes,
                    p.row_bytes, lane);
-    if (lane == 0) row_map[dst] = static_cast<int32_t>(src);
+    if (lane == 0) {
+      if (row_map != nullptr) row_map[dst] = static_cast<int32_t>(src);
+      if (peer_row_map != nullptr) {
+        const int64_t crow = min64(s_dst[s] + static_cast<int64_t>(j), p.comb_rows - 1);
+        peer_row_map[dst] = (s << kPeerRowBits) | static_cast<int32_t>(crow);
+      }
+    }
   }
   if (last_cta(p.ticket, &s_last) && threadIdx.x == 0) {
     *expect = s_target;
@@ -211,11 +224,13 @@ int launch_ep_dispatch(const EpParams& p, const void* send, const int32_t* slot_
              : -2;
 }
 
-int launch_ep_collect(const EpParams& p, void* xe, int32_t* row_map, int32_t* expert_offsets,
-                      uint32_t* expect, uint64_t timeout_ns, int64_t max_rows, cudaStream_t stream) {
+int launch_ep_collect(const EpParams& p, void* xe, int32_t* row_map, int32_t* peer_row_map,
+                      int32_t* expert_offsets, uint32_t* expect, uint64_t timeout_ns, int64_t max_rows,
+                      cudaStream_t stream) {
   const size_t smem = sizeof(int32_t) * (2 * p.G * p.P + p.G + 1 + p.P + 1);
   return launch_kernel(ep_collect_kernel, dim3(grid_for_rows(max_rows)), dim3(256), smem, stream, p,
-                       static_cast<uint8_t*>(xe), row_map, expert_offsets, expect, timeout_ns) == cudaSuccess
+                       static_cast<uint8_t*>(xe), row_map, peer_row_map, expert_offsets, expect,
+                       timeout_ns) == cudaSuccess
              ? 0
              : -2;
 }

@@ -71,7 +71,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + 
 template <int BN, int STAGES, bool SWIGLU, int BMA>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
-                        const __grid_constant__ CUtensorMap map_b, GemmParams p) {
+                        const __grid_constant__ CUtensorMap map_b, const __grid_constant__ GemmParams p) {
   using S = GemmShape<BN, STAGES, SWIGLU, BMA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -218,7 +218,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       const bool valid = warp_has_rows && r < rows;
       const int64_t grow = static_cast<int64_t>(off[e]) + r;
       int64_t orow = grow;
-      if (valid && p.out_row_map != nullptr) orow = p.out_row_map[grow];
+      __nv_bfloat16* peer_row = nullptr;
+      if (valid && p.peer_out)
+        peer_row = static_cast<__nv_bfloat16*>(peer_out_row(p.po, p.out_row_map[grow], p.ldo * 2));
+      else if (valid && p.out_row_map != nullptr)
+        orow = p.out_row_map[grow];
       int ok = 0;
       if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -226,7 +230,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       tc_fence_after();
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      __nv_bfloat16* orow_ptr = out + orow * p.ldo;
+      __nv_bfloat16* orow_ptr = p.peer_out ? peer_row : out + orow * p.ldo;
       if (!warp_has_rows) {
         // nothing of this tile lives in this warp's TMEM lanes
       } else if (SWIGLU) {
@@ -293,6 +297,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+  if (p.peer_out) {
+    __shared__ int s_last;
+    peer_out_publish(p.po, &s_last);
   }
 }
 

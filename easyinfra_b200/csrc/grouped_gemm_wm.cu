@@ -56,7 +56,7 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 template <int NTOK, int STAGES, bool SWIGLU>
 __global__ void __launch_bounds__(WM_THREADS, 1)
     grouped_gemm_wm_kernel(const __grid_constant__ CUtensorMap map_w,
-                           const __grid_constant__ CUtensorMap map_x, GemmParams p) {
+                           const __grid_constant__ CUtensorMap map_x, const __grid_constant__ GemmParams p) {
   using S = WmShape<NTOK, STAGES, SWIGLU>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -236,8 +236,14 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
         if (col < p.N) {
           for (int j = 0; j < ntok; ++j) {
             int64_t grow = static_cast<int64_t>(off[e]) + tok0 + j;
-            if (p.out_row_map != nullptr) grow = p.out_row_map[grow];
-            out[grow * p.ldo + col] = __float2bfloat16_rn(__uint_as_float(v[j]));
+            __nv_bfloat16* dst;
+            if (p.peer_out) {
+              dst = static_cast<__nv_bfloat16*>(peer_out_row(p.po, p.out_row_map[grow], p.ldo * 2));
+            } else {
+              if (p.out_row_map != nullptr) grow = p.out_row_map[grow];
+              dst = out + grow * p.ldo;
+            }
+            dst[col] = __float2bfloat16_rn(__uint_as_float(v[j]));
           }
         }
       }
@@ -252,6 +258,10 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+  if (p.peer_out) {
+    __shared__ int s_last;
+    peer_out_publish(p.po, &s_last);
   }
 }
 

@@ -212,6 +212,31 @@ struct AddNormParams {
 };
 
 // ---- grouped GEMM (grouped_gemm.cu)
+// Peer output of the down GEMM (fused combine-send): out_row_map[r] = (s << 24) | row
+// sends row r to row `row` of rank s's combine region; after the last tile every CTA
+// fences at system scope and the last one adds 1 to flags[G + rank] of every rank.
+struct PeerOut {
+  uint8_t* base[EP_MAX_RANKS];  // every rank's exchange buffer (flags at offset 0)
+  uint8_t* rows[EP_MAX_RANKS];  // every rank's combine region
+  int G = 0, rank = 0;
+  uint32_t* ticket = nullptr;   // local, zero between launches
+};
+constexpr int kPeerRowBits = 24;
+
+__device__ __forceinline__ void* peer_out_row(const PeerOut& po, int32_t v, int64_t ld_bytes) {
+  return po.rows[static_cast<uint32_t>(v) >> kPeerRowBits] +
+         static_cast<int64_t>(v & ((1 << kPeerRowBits) - 1)) * ld_bytes;
+}
+
+// End of a peer-output GEMM, run by every thread of every CTA.
+__device__ __forceinline__ void peer_out_publish(const PeerOut& po, int* s_last) {
+  if (last_cta(po.ticket, s_last) && threadIdx.x < po.G) {
+    __threadfence_system();
+    atomicAdd_system(ep_flags(po.base[threadIdx.x]) + po.G + po.rank, 1u);
+    if (threadIdx.x == 0) *po.ticket = 0u;
+  }
+}
+
 struct GemmParams {
   const int32_t* expert_offsets;  // [P+1]: rows of expert p are [off[p], off[p+1])
   int P;
@@ -223,6 +248,8 @@ struct GemmParams {
   int64_t ldo;  // elements
   const int32_t* out_row_map;  // null, or output row for every input row
   int* status;
+  int peer_out = 0;            // 1: rows go to other ranks (PeerOut), out is unused
+  PeerOut po;
 };
 
 // Grouped-GEMM kernel choice: automatic (by rows per slot), or forced for tests.
@@ -263,8 +290,9 @@ struct GemmF32Params {
 
 int launch_ep_dispatch(const EpParams& p, const void* send, const int32_t* slot_offsets, int64_t max_rows,
                        cudaStream_t stream);
-int launch_ep_collect(const EpParams& p, void* xe, int32_t* row_map, int32_t* expert_offsets,
-                      uint32_t* expect, uint64_t timeout_ns, int64_t max_rows, cudaStream_t stream);
+int launch_ep_collect(const EpParams& p, void* xe, int32_t* row_map, int32_t* peer_row_map,
+                      int32_t* expert_offsets, uint32_t* expect, uint64_t timeout_ns, int64_t max_rows,
+                      cudaStream_t stream);
 int launch_ep_combine_send(const EpParams& p, const void* y_recv, int64_t max_rows, cudaStream_t stream);
 int launch_ep_wait_comb(const EpParams& p, uint32_t* expect, uint64_t timeout_ns, cudaStream_t stream);
 

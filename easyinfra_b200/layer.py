@@ -135,9 +135,7 @@ class MoELayer:
             raise ValueError("gate_w rows must be E (+1 with a shared-expert gate)")
 
     # ------------------------------------------------------------ ROUTING_DISPATCH
-    def route_and_permute(self, x: torch.Tensor) -> DispatchState:
-        T = x.shape[0]
-        E1 = self.p.gate_w.shape[0]
+    def route(self, x: torch.Tensor) -> ops.RouterOutput:
         l2p = self.log2phy if self.use_map else None
         rep = self.rep_count if self.use_map else None
         if self.scoring == "sigmoid_grouped":
@@ -151,8 +149,13 @@ class MoELayer:
                            gate_bias=self.p.gate_bias, scale=self.scale,
                            has_shared_gate=self.shared_gate, log2phy=l2p, rep_count=rep,
                            num_slots=self.G * self.P, workspace=self.ws, status=self.status)
-        perm = ops.permute(x, r, num_slots=self.G * self.P, E1=E1)
-        return DispatchState(T=T, route=r, perm=perm)
+        return r
+
+    def route_and_permute(self, x: torch.Tensor) -> DispatchState:
+        """Router + permute into a local send buffer (no exchange)."""
+        r = self.route(x)
+        perm = ops.permute(x, r, num_slots=self.G * self.P, E1=self.p.gate_w.shape[0])
+        return DispatchState(T=x.shape[0], route=r, perm=perm)
 
     def exchange_counts(self, st: DispatchState) -> np.ndarray:
         """All-gather of per-slot counts ([G src, G*P] int32) and the one host sync
@@ -233,36 +236,57 @@ class MoELayer:
         return ro, self.forward(normed, out=out)
 
     # ------------------------------------------------------------ NVLink transport
-    def peer_dispatch(self, st: DispatchState) -> None:
-        self.exchange.dispatch(st.perm.send, st.route.slot_offsets, st.T * self.top_k)
+    def _fused(self) -> bool:
+        # the fused forms run the bf16 tensor-core kernels; fp32 layers use the plain ones
+        return self.exchange.fused and self.p.w_down.dtype == torch.bfloat16
+
+    def peer_route_dispatch(self, x: torch.Tensor) -> DispatchState:
+        """Router, then the rows to their owners: fused permute+dispatch, or permute into
+        the send buffer and a separate dispatch."""
+        xg = self.exchange
+        if self._fused():
+            r = self.route(x)
+            pos_of = xg.permute_dispatch(x, r, self.p.gate_w.shape[0])
+            return DispatchState(T=x.shape[0], route=r, perm=ops.PermuteOutput(None, pos_of, None, None))
+        st = self.route_and_permute(x)
+        xg.dispatch(st.perm.send, st.route.slot_offsets, st.T * self.top_k)
+        return st
 
     def peer_experts(self, st: DispatchState) -> None:
-        """Collect the rows of every source, run both GEMMs (the down GEMM writes back
-        into the receive region, in arrival order) and send the rows home."""
+        """Collect the rows of every source and run both GEMMs.  Fused: the down GEMM's
+        epilogue stores every row into the combine region of the rank that sent it.
+        Plain: the down GEMM writes back into the receive region (arrival order) and a
+        combine-send kernel returns the rows."""
         xg = self.exchange
         hint = st.T * self.top_k
-        xe, row_map, offs = xg.collect(rows_hint=hint)
+        fused = self._fused()
+        xe, row_map, offs = xg.collect(rows_hint=hint, peer_rows=fused)
         act = ops.grouped_swiglu(xe, offs, self.p.w_gate_up, out=xg.act, status=self.status, rows_hint=hint)
+        if fused:
+            xg.grouped_down_send(act, offs, self.p.w_down, row_map, rows_hint=hint, status=self.status)
+            return
         y = ops.grouped_down(act, offs, self.p.w_down, out=xg.recv, out_row_map=row_map,
                              status=self.status, rows_hint=hint)
         xg.combine_send(y, rows_hint=hint)
 
     def peer_finish(self, st: DispatchState, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self._fused():
+            return self.exchange.combine(st.perm.pos_of, st.route.topk_weights, shared=st.shared_out,
+                                         shared_gate=st.route.shared_gate, out=out)
         back = self.exchange.wait_combine(st.T * self.top_k)
         return self.unpermute(st, back, out)
 
-    def forward_peer(self, x: torch.Tensor, st: DispatchState,
-                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        self.peer_dispatch(st)
+    def forward_peer(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        st = self.peer_route_dispatch(x)
         self.shared_expert(x, st)  # overlaps the other ranks' rows arriving
         self.peer_experts(st)
         return self.peer_finish(st, out)
 
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Routed output plus the (gated) shared-expert output for this rank's tokens."""
-        st = self.route_and_permute(x)
         if self.G > 1 and self.exchange is not None:
-            return self.forward_peer(x, st, out)
+            return self.forward_peer(x, out)
+        st = self.route_and_permute(x)
         self.shared_expert(x, st)
         if self.G == 1:
             y = self.experts_local(st)
@@ -309,9 +333,7 @@ def forward_peer_single_device(layers: List[MoELayer], xs: List[torch.Tensor]) -
     """The NVLink transport with all G ranks in one process on one device: every layer
     carries a PeerExchange from PeerExchange.local_group, and each stage runs for all
     ranks before the next one starts, so every flag a kernel checks is already set."""
-    sts = [l.route_and_permute(x) for l, x in zip(layers, xs)]
-    for l, st in zip(layers, sts):
-        l.peer_dispatch(st)
+    sts = [l.peer_route_dispatch(x) for l, x in zip(layers, xs)]
     for l, x, st in zip(layers, xs, sts):
         l.shared_expert(x, st)
     for l, st in zip(layers, sts):

@@ -58,13 +58,14 @@ class PeerExchange:
     def __init__(self, *, world_size: int, rank: int, slots_per_rank: int, hidden: int, inter: int,
                  dtype: torch.dtype, max_tokens: int, top_k: int, device: torch.device,
                  buffer_ptr: int, peers: List[int], owns_buffer: bool, opened: List[int],
-                 timeout_s: float, status: Optional[torch.Tensor]):
+                 timeout_s: float, status: Optional[torch.Tensor], fused: bool = True):
         if world_size > _lib.EP_MAX_RANKS:
             raise ValueError(f"peer exchange supports at most {_lib.EP_MAX_RANKS} ranks")
         self.G, self.rank, self.P = world_size, rank, slots_per_rank
         self.H, self.I, self.dtype, self.device = hidden, inter, dtype, device
         self.K = top_k
         self.max_tokens = max_tokens
+        self.fused = fused  # fused permute+dispatch, down GEMM+send, combine+wait
         esz = torch.tensor([], dtype=dtype).element_size()
         self.row_bytes = hidden * esz
         self.cap_rows = max_tokens * top_k
@@ -84,6 +85,7 @@ class PeerExchange:
         self.x_expert = torch.empty(rows, hidden, dtype=dtype, device=device)
         self.act = torch.empty(rows, inter, dtype=dtype, device=device)
         self.row_map = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.peer_row_map = torch.zeros(rows, dtype=torch.int32, device=device)
         self.expert_offsets = torch.zeros(slots_per_rank + 1, dtype=torch.int32, device=device)
         d = _lib.EpDesc()
         for g, ptr in enumerate(peers):
@@ -104,7 +106,8 @@ class PeerExchange:
     @classmethod
     def create(cls, comm, *, rank: int, world_size: int, slots_per_rank: int, hidden: int, inter: int,
                dtype: torch.dtype, max_tokens: int, top_k: int, device: torch.device,
-               timeout_s: float = 10.0, status: Optional[torch.Tensor] = None) -> "PeerExchange":
+               timeout_s: float = 10.0, status: Optional[torch.Tensor] = None,
+               fused: bool = True) -> "PeerExchange":
         """Collective over `comm` (a GroupCommunicator of the node's ranks): allocate this
         rank's buffer, all-gather the IPC handles, map every peer's buffer."""
         nbytes = cls._sizes(world_size, slots_per_rank, hidden, dtype, max_tokens, top_k)
@@ -142,12 +145,12 @@ class PeerExchange:
         return cls(world_size=world_size, rank=rank, slots_per_rank=slots_per_rank, hidden=hidden,
                    inter=inter, dtype=dtype, max_tokens=max_tokens, top_k=top_k, device=device,
                    buffer_ptr=buf.value, peers=peers, owns_buffer=True, opened=opened,
-                   timeout_s=timeout_s, status=status)
+                   timeout_s=timeout_s, status=status, fused=fused)
 
     @classmethod
     def local_group(cls, *, world_size: int, slots_per_rank: int, hidden: int, inter: int,
                     dtype: torch.dtype, max_tokens: int, top_k: int, device: torch.device,
-                    status: Optional[torch.Tensor] = None) -> List["PeerExchange"]:
+                    status: Optional[torch.Tensor] = None, fused: bool = True) -> List["PeerExchange"]:
         """All ranks of a node in one process on one device: waits check their flags
         once (timeout 0), so the launches must be issued in stage order."""
         nbytes = cls._sizes(world_size, slots_per_rank, hidden, dtype, max_tokens, top_k)
@@ -161,7 +164,7 @@ class PeerExchange:
         return [cls(world_size=world_size, rank=r, slots_per_rank=slots_per_rank, hidden=hidden,
                     inter=inter, dtype=dtype, max_tokens=max_tokens, top_k=top_k, device=device,
                     buffer_ptr=bufs[r], peers=bufs, owns_buffer=True, opened=[], timeout_s=0.0,
-                    status=status) for r in range(world_size)]
+                    status=status, fused=fused) for r in range(world_size)]
 
     def close(self, comm=None) -> None:
         """Unmap peers and free this rank's buffer.  With `comm`, synchronise the device
@@ -195,13 +198,16 @@ class PeerExchange:
                   slot_offsets.data_ptr(), send_rows, ops._stream())
         ops._count(1)
 
-    def collect(self, rows_hint: int = 0):
-        """Wait for every source, regroup expert-major.  Returns (x_expert, row_map,
-        expert_offsets) — device buffers owned by the exchange."""
-        _lib.call("b200moe_ep_collect", self._p(), self.x_expert.data_ptr(), self.row_map.data_ptr(),
+    def collect(self, rows_hint: int = 0, peer_rows: bool = False):
+        """Wait for every source, regroup expert-major.  Returns (x_expert, row map,
+        expert_offsets) — device buffers owned by the exchange; the row map holds arrival
+        rows, or (peer_rows) (source << 24) | combine row at the source."""
+        rm = self.peer_row_map if peer_rows else self.row_map
+        _lib.call("b200moe_ep_collect", self._p(), self.x_expert.data_ptr(),
+                  None if peer_rows else rm.data_ptr(), rm.data_ptr() if peer_rows else None,
                   self.expert_offsets.data_ptr(), rows_hint, ops._stream())
         ops._count(1)
-        return self.x_expert, self.row_map, self.expert_offsets
+        return self.x_expert, rm, self.expert_offsets
 
     def combine_send(self, y_recv: torch.Tensor, rows_hint: int = 0) -> None:
         _lib.call("b200moe_ep_combine_send", self._p(), y_recv.data_ptr(), rows_hint, ops._stream())
@@ -212,3 +218,49 @@ class PeerExchange:
         _lib.call("b200moe_ep_wait_combine", self._p(), ops._stream())
         ops._count(1)
         return self.comb[:send_rows]
+
+    # ------------------------------------------------------------ fused forms
+    def permute_dispatch(self, x: torch.Tensor, r: "ops.RouterOutput", E1: int) -> torch.Tensor:
+        """Permute fused with the dispatch: token rows go straight to their owners.
+        Returns pos_of [T, K] (send positions, for combine)."""
+        ops._need_cuda(x)
+        x = ops._rows_contig(x)
+        T, H = x.shape
+        K = r.phys_ids.shape[1]
+        pos_of = torch.empty(T, K, dtype=torch.int32, device=x.device)
+        _lib.call("b200moe_ep_permute_dispatch", self._p(), x.data_ptr() if T else None, x.stride(0),
+                  ops._dtype_code(x), T, H, K, E1, r.phys_ids.data_ptr() if T else None,
+                  r.slot_offsets.data_ptr(), pos_of.data_ptr() if T else None, r.workspace.data_ptr(),
+                  r.workspace.numel(), ops._stream())
+        ops._count(1)
+        return pos_of
+
+    def grouped_down_send(self, act: torch.Tensor, expert_offsets: torch.Tensor, w_down: torch.Tensor,
+                          peer_row_map: torch.Tensor, rows_hint: int = 0,
+                          status: Optional[torch.Tensor] = None) -> None:
+        """Down GEMM whose epilogue stores each row into its source's combine region."""
+        P, H, I = w_down.shape
+        ops._hook("grouped_down", "start")
+        _lib.call("b200moe_ep_grouped_down_send", self._p(), act.data_ptr(), act.stride(0), act.shape[0],
+                  rows_hint, expert_offsets.data_ptr(), P, H, I, w_down.data_ptr(), peer_row_map.data_ptr(),
+                  ops._ptr(status), ops._stream())
+        ops._hook("grouped_down", "end")
+        ops._count(1)
+
+    def combine(self, pos_of: torch.Tensor, topk_weights: torch.Tensor, *,
+                shared: Optional[torch.Tensor] = None, shared_gate: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Wait for this rank's rows (bounded, inside the kernel), then the weighted unpermute."""
+        T, K = pos_of.shape
+        o = out if out is not None else torch.empty(T, self.H, dtype=self.dtype, device=self.device)
+        if shared is not None:
+            shared = ops._rows_contig(shared)
+        if shared_gate is not None:
+            shared_gate = shared_gate.to(torch.float32).contiguous()
+        w = topk_weights.to(torch.float32).contiguous()
+        _lib.call("b200moe_ep_combine", self._p(), pos_of.data_ptr() if T else None,
+                  w.data_ptr() if T else None, T, K, self.H, ops._DT[self.dtype], ops._ptr(shared),
+                  shared.stride(0) if shared is not None else 0, ops._ptr(shared_gate),
+                  o.data_ptr() if T else None, o.stride(0) if T else self.H, ops._stream())
+        ops._count(1)
+        return o

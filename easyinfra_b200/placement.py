@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import json
 import os
-from typing import Dict, Optional, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
@@ -65,6 +65,27 @@ class Placement:
         if len(m) % ep_size:
             raise ValueError(f"{len(m)} physical slots do not divide over {ep_size} ranks")
         return cls(torch.tensor(m, dtype=torch.long).view(ep_size, -1), num_logical)
+
+    # ---------------------------------------------------------------- weight loading
+    def local_slots_of(self, logical_expert: int, rank: int) -> List[int]:
+        """Local slot ids p of `rank` that hold `logical_expert` ([] if none), in slot
+        order (logical_to_physical_expert_ids, blocks/moe/base.py:25-37)."""
+        return [p for p, e in enumerate(self.phy2log[rank].tolist()) if e == logical_expert]
+
+    def physical_param_names(self, param_name: str, rank: int) -> List[str]:
+        """Checkpoint parameter name of a logical expert -> the names of this rank's
+        physical copies, for the experts' weight_loader (the contract of
+        get_physical_expert_module_names, modeling_utils/causal_lm.py:349-378):
+        "...experts.experts.<logical>.<proj>.weight" becomes one name per local slot
+        holding that expert, with <logical> replaced by the local slot id.  [] means the
+        expert is not placed on this rank and the tensor is skipped."""
+        head, sep, tail = param_name.partition("experts.experts.")
+        if not sep:
+            raise ValueError(f"{param_name!r} is not an expert parameter")
+        eid, dot, rest = tail.partition(".")
+        if not dot or not eid.isdigit():
+            raise ValueError(f"{param_name!r} has no expert id after 'experts.experts.'")
+        return [f"{head}experts.experts.{p}.{rest}" for p in self.local_slots_of(int(eid), rank)]
 
     # ---------------------------------------------------------------- queries
     @property

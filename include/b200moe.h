@@ -330,11 +330,45 @@ B200MOE_API int b200moe_ep_free(void* buffer);
 
 B200MOE_API int b200moe_ep_dispatch(const b200moe_ep_desc* ep, const void* send, const int32_t* slot_offsets,
                                     int64_t send_rows, void* stream);
+/* row_map (nullable): arrival row of every expert-major row, for b200moe_grouped_down's
+ * out_row_map; peer_row_map (nullable): (source rank << 24) | row in that rank's
+ * combine region, for b200moe_ep_grouped_down_send.  At least one of the two. */
 B200MOE_API int b200moe_ep_collect(const b200moe_ep_desc* ep, void* x_expert, int32_t* row_map,
-                                   int32_t* expert_offsets, int64_t rows_hint, void* stream);
+                                   int32_t* peer_row_map, int32_t* expert_offsets, int64_t rows_hint,
+                                   void* stream);
 B200MOE_API int b200moe_ep_combine_send(const b200moe_ep_desc* ep, const void* y_recv, int64_t rows_hint,
                                         void* stream);
 B200MOE_API int b200moe_ep_wait_combine(const b200moe_ep_desc* ep, void* stream);
+
+/*
+ * Fused forms of the exchange (same protocol, fewer launches and HBM passes):
+ *   b200moe_ep_permute_dispatch   b200moe_permute + b200moe_ep_dispatch: each token row
+ *                                 is read once and stored straight into the owning
+ *                                 ranks' receive regions (no send buffer); pos_of as in
+ *                                 b200moe_permute (send positions, for the combine).
+ *                                 slot_offsets and workspace are the router call's.
+ *                                 Launched even when T == 0 (it publishes empty counts).
+ *   b200moe_ep_grouped_down_send  b200moe_grouped_down + b200moe_ep_combine_send: the
+ *                                 epilogue stores each output row into the combine
+ *                                 region of the rank that sent it (peer_row_map from
+ *                                 b200moe_ep_collect), so the NVLink stores overlap the
+ *                                 tensor-core work; the last CTA raises the flags.
+ *   b200moe_ep_combine            b200moe_ep_wait_combine + b200moe_combine on this rank's
+ *                                 combine region: every CTA waits (bounded) for the
+ *                                 flags, then gathers; always launched (it consumes the
+ *                                 flags even when T == 0).
+ */
+B200MOE_API int b200moe_ep_permute_dispatch(const b200moe_ep_desc* ep, const void* x, int64_t ldx, int x_dtype,
+                                            int T, int H, int K, int E1, const int32_t* phys_ids,
+                                            const int32_t* slot_offsets, int32_t* pos_of, void* workspace,
+                                            size_t workspace_bytes, void* stream);
+B200MOE_API int b200moe_ep_grouped_down_send(const b200moe_ep_desc* ep, const void* act, int64_t ld_act,
+                                             int64_t rows_cap, int64_t rows_hint, const int32_t* expert_offsets,
+                                             int P, int H, int I, const void* w_down,
+                                             const int32_t* peer_row_map, int* status, void* stream);
+B200MOE_API int b200moe_ep_combine(const b200moe_ep_desc* ep, const int32_t* pos_of, const float* topk_w, int T,
+                                   int K, int H, int dtype, const void* shared, int64_t lds,
+                                   const float* shared_gate, void* out, int64_t ldo, void* stream);
 
 #ifdef __cplusplus
 }

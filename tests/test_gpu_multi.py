@@ -64,12 +64,12 @@ def _worker(rank, world, port, case_name, transport, q):
         xs = [C.hidden_states(shape, T, rank=r) for r in range(world)]
         xg = None
         same_as_nccl = True
-        if transport == "nvlink":
+        if transport.startswith("nvlink"):
             from easyinfra_b200.peer_exchange import PeerExchange
             out_nccl = lay.forward(xs[rank].to(dev))
             xg = PeerExchange.create(comm, rank=rank, world_size=world, slots_per_rank=P, hidden=lay.H,
                                      inter=lay.I, dtype=shape.dtype, max_tokens=T, top_k=shape.top_k,
-                                     device=dev, timeout_s=5.0)
+                                     device=dev, timeout_s=5.0, fused=transport == "nvlink")
             lay.exchange = xg
         out = lay.forward(xs[rank].to(dev))
         out2 = lay.forward(xs[rank].to(dev))     # second call: buffers and tables reused
@@ -109,7 +109,7 @@ def _worker(rank, world, port, case_name, transport, q):
         q.put((rank, None, None, None, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("transport", ["nccl", "nvlink"])
+@pytest.mark.parametrize("transport", ["nccl", "nvlink", "nvlink_plain"])
 @pytest.mark.parametrize("case_name", ["mixtral_g2", "qwen3_g8", "dsv2_g2"])
 def test_ep_layer_multi_gpu(case_name, transport):
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:

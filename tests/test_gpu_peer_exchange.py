@@ -49,11 +49,11 @@ def _layers(case, device, status, gate_bias_override=None):
     return shape, layers
 
 
-def _attach(layers, shape, max_tokens, device, status):
+def _attach(layers, shape, max_tokens, device, status, fused):
     lay = layers[0]
     xgs = PeerExchange.local_group(world_size=lay.G, slots_per_rank=lay.P, hidden=lay.H, inter=lay.I,
                                    dtype=shape.dtype, max_tokens=max_tokens, top_k=shape.top_k,
-                                   device=device, status=status)
+                                   device=device, status=status, fused=fused)
     for l, xg in zip(layers, xgs):
         l.exchange = xg
     return xgs
@@ -70,15 +70,16 @@ def _nccl_path(layers, xs):
             l.exchange = xg
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "plain"])
 @pytest.mark.parametrize("name", EP_CASES)
-def test_peer_exchange_matches_host_planned_path(cuda_device, name):
+def test_peer_exchange_matches_host_planned_path(cuda_device, name, fused):
     case = cases.CASES[name]
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
     shape, layers = _layers(case, cuda_device, status)
     T = case["T"]
     xs = [C.hidden_states(shape, T, rank=r).to(cuda_device) for r in range(case["G"])]
     ref = _nccl_path(layers, xs)
-    xgs = _attach(layers, shape, T, cuda_device, status)
+    xgs = _attach(layers, shape, T, cuda_device, status, fused)
     try:
         for it in range(3):   # flags and arrival counters advance call after call
             outs = forward_peer_single_device(layers, xs)
@@ -86,15 +87,17 @@ def test_peer_exchange_matches_host_planned_path(cuda_device, name):
             assert int(status.item()) == 0, f"status {int(status.item())} on call {it}"
             for r in range(case["G"]):
                 assert torch.equal(outs[r], ref[r]), (name, it, r)
-        c = xgs[0].counters.cpu().tolist()
-        assert c[:3] == [0, 0, 0], "tickets must return to zero"
-        assert c[3] == 3 and c[4] == 3, c
+        for xg in xgs:
+            c = xg.counters.cpu().tolist()
+            assert c[:3] == [0, 0, 0] and c[5:] == [0, 0, 0], f"tickets must return to zero: {c}"
+            assert c[3] == 3 and c[4] == 3, c
     finally:
         for xg in xgs:
             xg.close()
 
 
-def test_peer_exchange_rank_without_tokens(cuda_device):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "plain"])
+def test_peer_exchange_rank_without_tokens(cuda_device, fused):
     case = cases.CASES["mixtral_g2"]
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
     shape, layers = _layers(case, cuda_device, status)
@@ -102,7 +105,7 @@ def test_peer_exchange_rank_without_tokens(cuda_device):
     xs = [C.hidden_states(shape, T, rank=0).to(cuda_device),
           C.hidden_states(shape, T, rank=1)[:0].to(cuda_device)]
     ref = _nccl_path(layers, xs)
-    xgs = _attach(layers, shape, T, cuda_device, status)
+    xgs = _attach(layers, shape, T, cuda_device, status, fused)
     try:
         outs = forward_peer_single_device(layers, xs)
         torch.cuda.synchronize()
@@ -114,7 +117,8 @@ def test_peer_exchange_rank_without_tokens(cuda_device):
             xg.close()
 
 
-def test_peer_exchange_all_rows_to_one_rank(cuda_device):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "plain"])
+def test_peer_exchange_all_rows_to_one_rank(cuda_device, fused):
     """Worst-case routing: a large bias sends every token's top-k to experts that only
     rank 0 holds, so rank 0 receives G * T * K rows (the full capacity)."""
     case = cases.CASES["qwen15_g4"]
@@ -133,7 +137,7 @@ def test_peer_exchange_all_rows_to_one_rank(cuda_device):
     T = case["T"]
     xs = [C.hidden_states(shape, T, rank=r).to(cuda_device) for r in range(case["G"])]
     ref = _nccl_path(layers, xs)
-    xgs = _attach(layers, shape, T, cuda_device, status)
+    xgs = _attach(layers, shape, T, cuda_device, status, fused)
     try:
         outs = forward_peer_single_device(layers, xs)
         torch.cuda.synchronize()
@@ -162,6 +166,13 @@ def test_wait_that_runs_out_reports_timeout(cuda_device):
         status.zero_()
         xgs[1].desc.timeout_ns = 1_000_000
         xgs[1].wait_combine(0)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 1
+        status.zero_()
+        # the combine that waits inside the kernel: every CTA gives up, none hangs
+        pos = torch.zeros(4, 2, dtype=torch.int32, device=cuda_device)
+        w = torch.ones(4, 2, dtype=torch.float32, device=cuda_device)
+        xgs[1].combine(pos, w)
         torch.cuda.synchronize()
         assert int(status.item()) == 1
         assert torch.ones(4, device=cuda_device).sum().item() == 4.0

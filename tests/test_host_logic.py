@@ -87,3 +87,20 @@ def test_synthetic_generators_deterministic():
     assert 0.6 <= s0 <= 1.4 and 0.6 <= s1 <= 1.4 and s0 != s1
     gb = C.gate_bias(sh, 0)
     assert gb.shape == (128,) and float(gb.max()) == 0.0
+
+
+def test_physical_param_names_follow_the_placement():
+    """Checkpoint names of logical experts map to this rank's physical slots (replicas
+    give several names, experts held elsewhere none), as the reference's
+    get_physical_expert_module_names does."""
+    from easyinfra_b200.placement import Placement
+    pl = Placement(torch.tensor([[0, 1, 2, 0], [3, 1, 2, 3]]), 4)
+    n = "model.layers.3.mlp.experts.experts.{}.gate_proj.weight"
+    assert pl.physical_param_names(n.format(0), 0) == [n.format(0), n.format(3)]
+    assert pl.physical_param_names(n.format(0), 1) == []
+    assert pl.physical_param_names(n.format(3), 1) == [n.format(0), n.format(3)]
+    assert pl.physical_param_names(n.format(1), 1) == [n.format(1)]
+    assert pl.local_slots_of(2, 0) == [2]
+    import pytest
+    with pytest.raises(ValueError):
+        pl.physical_param_names("model.layers.3.mlp.gate.weight", 0)
