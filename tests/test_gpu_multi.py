@@ -109,12 +109,7 @@ def _worker(rank, world, port, case_name, transport, q):
         q.put((rank, None, None, None, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("transport", ["nccl", "nvlink", "nvlink_plain"])
-@pytest.mark.parametrize("case_name", ["mixtral_g2", "qwen3_g8", "dsv2_g2"])
-def test_ep_layer_multi_gpu(case_name, transport):
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+def _run(case_name, transport, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -130,3 +125,19 @@ def test_ep_layer_multi_gpu(case_name, transport):
         assert err < 6e-3, (rank, err)
         assert rep, "repeated calls, transports or graph replays gave different outputs"
         assert excluded <= 2
+
+
+@pytest.mark.parametrize("transport", ["nccl", "nvlink", "nvlink_plain"])
+@pytest.mark.parametrize("case_name", ["mixtral_g2", "qwen3_g8", "dsv2_g2"])
+def test_ep_layer_multi_gpu(case_name, transport):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run(case_name, transport, 2)
+
+
+@pytest.mark.parametrize("transport", ["nccl", "nvlink"])
+def test_ep_layer_eight_gpus(transport):
+    """The Qwen3 160-slot EasyBalance map at its native EP size (8 ranks)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 8:
+        pytest.skip("needs 8 GPUs")
+    _run("qwen3_g8", transport, 8)
