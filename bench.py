@@ -60,6 +60,10 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (invalid as a result)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="also replay one step with CUDA events around every library call and "
+                         "report the device time per entry point and layer (events between the "
+                         "launches cost a few microseconds each and break launch overlap)")
     ap.add_argument("--transport", default="nvlink", choices=["nvlink", "nvlink_plain", "nccl"],
                     help="expert-parallel row exchange for --gpus > 1: peer memory with the fused "
                          "kernels (graph-captured), peer memory with separate exchange kernels, or "
@@ -355,6 +359,8 @@ def run_ours(args):
                "launches": launches, "clocks": clocks, "graph": use_graph}
         if use_graph:
             del graph, run
+        if args.breakdown and with_roofline:
+            res["breakdown_us_per_layer"] = op_breakdown(stack, T, x, use_graph, barrier, len(layers))
         if with_roofline and kernel_ms and layer_rows[0] is not None:
             # algorithmic work of the SwiGLU GEMM per launch, averaged over layers
             H, I = shape.hidden, shape.intermediate
@@ -417,11 +423,47 @@ def run_ours(args):
         "clocks": main["clocks"],
         "secondary": secondary,
     }
+    if "breakdown_us_per_layer" in main:
+        line["breakdown_us_per_layer"] = main["breakdown_us_per_layer"]
     if exchange_status:
         line["exchange_status"] = exchange_status   # a bounded wait gave up: numbers invalid
     if args.layers:
         line["config"]["debug_reduced_layers"] = True
     print(json.dumps(line), flush=True)
+
+
+def op_breakdown(stack, T, x, use_graph, barrier, n_layers):
+    """Device time per library entry point, per layer: one step (captured like the timed
+    steps when they are graphs) with CUDA events recorded around every call."""
+    import collections
+    from easyinfra_b200 import _lib
+    events = []
+
+    def hook(name, phase):
+        e = torch.cuda.Event(enable_timing=True, external=use_graph)
+        e.record()
+        events.append((name, phase, e))
+
+    if use_graph:
+        def arm():
+            events.clear()
+            _lib.CALL_HOOK["fn"] = hook
+        graph = stack.capture(T, on_capture=arm)
+        _lib.CALL_HOOK["fn"] = None
+        graph(x)               # warm replay
+        barrier()
+        torch.cuda.synchronize()
+        graph(x)
+    else:
+        _lib.CALL_HOOK["fn"] = hook
+        stack.forward(x)
+        _lib.CALL_HOOK["fn"] = None
+    torch.cuda.synchronize()
+    per = collections.defaultdict(float)
+    for (name, _, e0), (_, _, e1) in zip(events[0::2], events[1::2]):
+        per[name] += e0.elapsed_time(e1) * 1000.0
+    barrier()
+    return {k: round(v / n_layers, 2) for k, v in per.items()}
 
 
 def traffic_for(workload: str):

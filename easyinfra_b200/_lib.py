@@ -175,10 +175,21 @@ def load() -> ctypes.CDLL:
     return _lib
 
 
+# Optional callable(name, "start" | "end") invoked around every entry-point call (on the
+# caller's thread, so it can record CUDA events on the launching stream); bench.py
+# uses it for its per-op breakdown.
+CALL_HOOK = {"fn": None}
+
+
 def call(name: str, *args) -> None:
     """Invoke an entry point; raise B200MoEError with the library's message on failure."""
     lib = load()
+    hook = CALL_HOOK["fn"]
+    if hook is not None:
+        hook(name, "start")
     rc = getattr(lib, name)(*args)
+    if hook is not None:
+        hook(name, "end")
     if rc != 0:
         msg = lib.b200moe_last_error().decode(errors="replace")
         raise B200MoEError(f"{name} failed ({rc}): {msg}")

@@ -54,7 +54,15 @@ __global__ void __launch_bounds__(256) gather_segments_kernel(const uint8_t* src
   for (int r = r0 + warp; r < r1; r += blockDim.x >> 5) {
     const uint4* s = reinterpret_cast<const uint4*>(src + (static_cast<int64_t>(src_start[seg]) + r) * row_bytes);
     uint4* d = reinterpret_cast<uint4*>(dst + (static_cast<int64_t>(dst_start[seg]) + r) * row_bytes);
-    for (int64_t v = lane; v < vec; v += 32) d[v] = __ldg(s + v);
+    int64_t v = lane;
+    for (; v + 7 * 32 < vec; v += 8 * 32) {  // eight loads in flight per lane
+      uint4 t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = __ldg(s + v + u * 32);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) d[v + u * 32] = t[u];
+    }
+    for (; v < vec; v += 32) d[v] = __ldg(s + v);
     if (dst_to_src != nullptr && lane == 0) dst_to_src[dst_start[seg] + r] = src_start[seg] + r;
   }
 }
@@ -255,7 +263,7 @@ int b200moe_router(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
   lp.H = H;
   lp.E1 = E1;
   lp.logits = logits_out ? logits_out : ws.logits;
-  launch_router_logits(lp, x_dtype, st);
+  if (launch_router_logits(lp, x_dtype, st)) return fail(B200MOE_ECUDA, "router_logits: kernel setup failed");
   if ((rc = check_launch("router_logits"))) return rc;
   return select_common(lp.logits, has_shared_gate, T, E, K, renorm, scale,
                        x_dtype == B200MOE_DTYPE_BF16, log2phy, rep_count, max_rep, num_slots,
@@ -299,7 +307,7 @@ int b200moe_router_sigmoid_grouped(const void* x, int64_t ldx, int x_dtype, cons
   lp.E1 = E;
   lp.logits = logits_out ? logits_out : ws.logits;
   lp.round_bf16 = 0;  // the reference computes these logits in fp32
-  launch_router_logits(lp, x_dtype, st);
+  if (launch_router_logits(lp, x_dtype, st)) return fail(B200MOE_ECUDA, "router_logits: kernel setup failed");
   if ((rc = check_launch("router_logits"))) return rc;
   return select_common(lp.logits, 0, T, E, K, renorm && K > 1, scale, x_dtype == B200MOE_DTYPE_BF16,
                        log2phy, rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, nullptr,

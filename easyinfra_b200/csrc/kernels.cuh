@@ -111,13 +111,23 @@ __device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t tar
   }
 }
 
-// One warp copies one row; L2-only loads for rows that a peer wrote.
+// One warp copies one row; L2-only loads for rows that a peer wrote.  Eight loads per
+// lane are issued before their stores, so a row's reads are in flight together rather
+// than one latency per 512 bytes.
 template <bool FROM_PEER>
 __device__ __forceinline__ void copy_row(uint8_t* dst, const uint8_t* src, int row_bytes, int lane) {
   const uint4* s = reinterpret_cast<const uint4*>(src);
   uint4* d = reinterpret_cast<uint4*>(dst);
   const int n = row_bytes >> 4;
-  for (int v = lane; v < n; v += 32) d[v] = FROM_PEER ? __ldcg(s + v) : s[v];
+  int v = lane;
+  for (; v + 7 * 32 < n; v += 8 * 32) {
+    uint4 t[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) t[u] = FROM_PEER ? __ldcg(s + v + u * 32) : s[v + u * 32];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) d[v + u * 32] = t[u];
+  }
+  for (; v < n; v += 32) d[v] = FROM_PEER ? __ldcg(s + v) : s[v];
 }
 
 // Clamp a per-slot count so that the running sum never exceeds `cap`.

@@ -85,13 +85,20 @@ __global__ void __launch_bounds__(256) permute_rows(const __grid_constant__ Perm
   }
   if (PEER) __syncthreads();
 
-  // Row copies: one warp per token; the token row is read once and written K times.
+  // Row copies: one warp per token; the token row is read once (PM_BATCH 16-byte loads
+  // per lane in flight together) and written K times.
+  constexpr int PM_BATCH = 8;
   const int vec_per_row = p.row_bytes / 16;
   for (int lt = warp; lt < nt; lt += blockDim.x >> 5) {
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) +
                                                       static_cast<int64_t>(t0 + lt) * p.x_stride);
-    for (int v = lane; v < vec_per_row; v += 32) {
-      const uint4 val = __ldg(src + v);
+    for (int v0 = 0; v0 < vec_per_row; v0 += PM_BATCH * 32) {
+      uint4 val[PM_BATCH];
+#pragma unroll
+      for (int u = 0; u < PM_BATCH; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (v < vec_per_row) val[u] = __ldg(src + v);
+      }
       for (int k = 0; k < p.K; ++k) {
         uint4* dst;
         if (PEER) {
@@ -102,7 +109,11 @@ __global__ void __launch_bounds__(256) permute_rows(const __grid_constant__ Perm
           dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.send) +
                                          static_cast<int64_t>(pos[lt * p.K + k]) * p.row_bytes);
         }
-        dst[v] = val;
+#pragma unroll
+        for (int u = 0; u < PM_BATCH; ++u) {
+          const int v = v0 + u * 32 + lane;
+          if (v < vec_per_row) dst[v] = val[u];
+        }
       }
     }
   }
@@ -171,7 +182,8 @@ __device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
 
 // One warp per (token, 256-column chunk): all K expert rows of the chunk are loaded
 // before any arithmetic, so a token's gathers are in flight together.
-template <typename E, bool PEER>
+// KT: compile-time bound on K (registers scale with it: KT rows of 8 values in flight).
+template <typename E, bool PEER, int KT>
 __device__ __forceinline__ void combine_body(const CombineParams& p) {
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -181,10 +193,10 @@ __device__ __forceinline__ void combine_body(const CombineParams& p) {
   const int c = static_cast<int>(gw - static_cast<int64_t>(t) * chunks) * 256 + lane * 8;
   if (c >= p.H) return;
   const E* y = static_cast<const E*>(p.y);
-  float v[8][8];
-  float wts[8];
+  float v[KT][8];
+  float wts[KT];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < KT; ++k) {
     if (k < p.K) {
       const int row = p.pos_of[static_cast<int64_t>(t) * p.K + k];
       wts[k] = p.topk_w[static_cast<int64_t>(t) * p.K + k];
@@ -193,7 +205,7 @@ __device__ __forceinline__ void combine_body(const CombineParams& p) {
   }
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < KT; ++k) {
     if (k < p.K) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = fmaf(wts[k], v[k][i], acc[i]);
@@ -212,7 +224,7 @@ __device__ __forceinline__ void combine_body(const CombineParams& p) {
 // PEER: y is this rank's combine region, filled by the ranks that hold its experts.
 // Every CTA first waits (bounded) until each of them raised its flag past the count
 // this rank consumed; the last CTA to finish advances that count.
-template <typename E, bool PEER>
+template <typename E, bool PEER, int KT>
 __global__ void __launch_bounds__(256) combine_rows(const __grid_constant__ CombineParams p) {
   __shared__ uint32_t s_target;
   __shared__ int s_last;
@@ -228,7 +240,7 @@ __global__ void __launch_bounds__(256) combine_rows(const __grid_constant__ Comb
     }
     __syncthreads();
   }
-  combine_body<E, PEER>(p);
+  combine_body<E, PEER, KT>(p);
   if (PEER) {
     __syncthreads();
     if (threadIdx.x == 0) s_last = (atomicAdd(p.wait_ticket, 1u) == gridDim.x - 1);
@@ -252,6 +264,15 @@ int launch_permute(const PermuteParams& p, cudaStream_t stream) {
   return 0;
 }
 
+template <typename E, bool PEER>
+static cudaError_t launch_combine_k(const CombineParams& p, int grid, cudaStream_t stream) {
+  if (p.K <= 1) return launch_kernel(combine_rows<E, PEER, 1>, dim3(grid), dim3(256), 0, stream, p);
+  if (p.K <= 2) return launch_kernel(combine_rows<E, PEER, 2>, dim3(grid), dim3(256), 0, stream, p);
+  if (p.K <= 4) return launch_kernel(combine_rows<E, PEER, 4>, dim3(grid), dim3(256), 0, stream, p);
+  if (p.K <= 6) return launch_kernel(combine_rows<E, PEER, 6>, dim3(grid), dim3(256), 0, stream, p);
+  return launch_kernel(combine_rows<E, PEER, 8>, dim3(grid), dim3(256), 0, stream, p);
+}
+
 int launch_combine(const CombineParams& p, cudaStream_t stream) {
   const bool peer = p.wait_n > 0;
   if (p.T == 0 && !peer) return 0;  // peer mode always runs: it consumes the arrival flags
@@ -259,11 +280,10 @@ int launch_combine(const CombineParams& p, cudaStream_t stream) {
   const int grid = static_cast<int>(max64(1, (warps * 32 + 255) / 256));
   cudaError_t e;
   if (p.dtype == kDtypeBF16)
-    e = peer ? launch_kernel(combine_rows<__nv_bfloat16, true>, dim3(grid), dim3(256), 0, stream, p)
-             : launch_kernel(combine_rows<__nv_bfloat16, false>, dim3(grid), dim3(256), 0, stream, p);
+    e = peer ? launch_combine_k<__nv_bfloat16, true>(p, grid, stream)
+             : launch_combine_k<__nv_bfloat16, false>(p, grid, stream);
   else
-    e = peer ? launch_kernel(combine_rows<float, true>, dim3(grid), dim3(256), 0, stream, p)
-             : launch_kernel(combine_rows<float, false>, dim3(grid), dim3(256), 0, stream, p);
+    e = peer ? launch_combine_k<float, true>(p, grid, stream) : launch_combine_k<float, false>(p, grid, stream);
   return e == cudaSuccess ? 0 : -2;
 }
 

@@ -24,66 +24,81 @@
 namespace b200moe {
 
 // ------------------------------------------------------------------ logits (bf16)
-// CTA = 4 warps, 64 tokens.  x and W_gate chunks of 64 hidden elements are staged in
-// shared memory with a padded row stride; each warp owns 16 tokens and every
-// 8-expert column tile.
+// CTA = 4 warps, 64 tokens.  Chunks of 64 hidden elements of x and of the CTA's W_gate
+// rows stream through a RL_STAGES-deep cp.async ring in shared memory (padded row
+// stride), so the HBM reads of later chunks overlap the MMAs of the current one; each
+// warp owns 16 tokens and every 8-expert column tile (mma.sync m16n8k16, fp32 acc).
 constexpr int RL_TOK = 64;
 constexpr int RL_HC = 64;        // hidden elements per chunk
 constexpr int RL_LD = RL_HC + 8; // padded smem row (bf16 elements)
 constexpr int RL_MAXNT = 17;     // up to 136 logit columns per pass
 
-__global__ void __launch_bounds__(128) router_logits_bf16(RouterLogitsParams p, int cols_per_cta) {
+// RL_STAGES chunks in flight: 8 for narrow column groups (few router columns: the
+// kernel is a pure stream over x and needs the most bytes in flight), 4 otherwise.
+template <int RL_STAGES>
+__global__ void __launch_bounds__(128) router_logits_bf16(const __grid_constant__ RouterLogitsParams p,
+                                                          int cols_per_cta) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   pdl_trigger();
   pdl_wait();
 
   const int col0 = blockIdx.y * cols_per_cta;
   const int ncols = min(cols_per_cta, p.E1 - col0);
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw);     // [64][RL_LD]
-  __nv_bfloat16* ws = xs + RL_TOK * RL_LD;                             // [ncols_pad][RL_LD]
   const int nt = (ncols + 7) / 8;
   const int ncols_pad = nt * 8;
+  const int stage_elems = (RL_TOK + cols_per_cta) * RL_LD;
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * RL_TOK;
   const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(p.x);
   const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(p.w);
+  const int nchunks = (p.H + RL_HC - 1) / RL_HC;
+
+  auto load_chunk = [&](int c) {
+    __nv_bfloat16* xs = ring + (c % RL_STAGES) * stage_elems;
+    __nv_bfloat16* ws = xs + RL_TOK * RL_LD;
+    const int h0 = c * RL_HC;
+    for (int i = threadIdx.x; i < RL_TOK * 8; i += 128) {
+      const int r = i >> 3, cc = (i & 7) * 8;
+      const int t = tok0 + r;
+      const bool ok = t < p.T && h0 + cc < p.H;
+      cp_async_16(xs + r * RL_LD + cc, ok ? x + static_cast<int64_t>(t) * p.ldx + h0 + cc : x, ok);
+    }
+    for (int i = threadIdx.x; i < ncols_pad * 8; i += 128) {
+      const int r = i >> 3, cc = (i & 7) * 8;
+      const bool ok = r < ncols && h0 + cc < p.H;
+      cp_async_16(ws + r * RL_LD + cc, ok ? w + static_cast<int64_t>(col0 + r) * p.H + h0 + cc : w, ok);
+    }
+  };
 
   float acc[RL_MAXNT][4];
 #pragma unroll
   for (int i = 0; i < RL_MAXNT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
-  for (int h0 = 0; h0 < p.H; h0 += RL_HC) {
-    __syncthreads();
-    // stage x chunk: 64 rows x 64 bf16 = 8 x 16B per row
-    for (int i = threadIdx.x; i < RL_TOK * 8; i += 128) {
-      const int r = i >> 3, c = (i & 7) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      const int t = tok0 + r;
-      if (t < p.T && h0 + c < p.H) v = *reinterpret_cast<const uint4*>(x + t * p.ldx + h0 + c);
-      *reinterpret_cast<uint4*>(xs + r * RL_LD + c) = v;
-    }
-    for (int i = threadIdx.x; i < ncols_pad * 8; i += 128) {
-      const int r = i >> 3, c = (i & 7) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      const int e = col0 + r;
-      if (r < ncols && h0 + c < p.H) v = *reinterpret_cast<const uint4*>(w + static_cast<int64_t>(e) * p.H + h0 + c);
-      *reinterpret_cast<uint4*>(ws + r * RL_LD + c) = v;
-    }
-    __syncthreads();
-    const int ar = warp * 16 + (lane >> 2);
-    const int ac = (lane & 3) * 2;
+#pragma unroll
+  for (int c = 0; c < RL_STAGES - 1; ++c) {
+    if (c < nchunks) load_chunk(c);
+    cp_async_commit();
+  }
+  const int ar = warp * 16 + (lane >> 2);
+  const int ac = (lane & 3) * 2;
+  for (int c = 0; c < nchunks; ++c) {
+    cp_async_wait<RL_STAGES - 2>();  // chunk c has landed (this thread's copies)
+    __syncthreads();                 // ... and everyone's; chunk c-1's stage is free
+    const __nv_bfloat16* xs = ring + (c % RL_STAGES) * stage_elems;
+    const __nv_bfloat16* ws = xs + RL_TOK * RL_LD;
 #pragma unroll
     for (int k0 = 0; k0 < RL_HC; k0 += 16) {
-      uint32_t a0 = *reinterpret_cast<const uint32_t*>(xs + ar * RL_LD + k0 + ac);
-      uint32_t a1 = *reinterpret_cast<const uint32_t*>(xs + (ar + 8) * RL_LD + k0 + ac);
-      uint32_t a2 = *reinterpret_cast<const uint32_t*>(xs + ar * RL_LD + k0 + ac + 8);
-      uint32_t a3 = *reinterpret_cast<const uint32_t*>(xs + (ar + 8) * RL_LD + k0 + ac + 8);
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(xs + ar * RL_LD + k0 + ac);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(xs + (ar + 8) * RL_LD + k0 + ac);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(xs + ar * RL_LD + k0 + ac + 8);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(xs + (ar + 8) * RL_LD + k0 + ac + 8);
 #pragma unroll
       for (int j = 0; j < RL_MAXNT; ++j) {
         if (j < nt) {
           const int bn = j * 8 + (lane >> 2);
-          uint32_t b0 = *reinterpret_cast<const uint32_t*>(ws + bn * RL_LD + k0 + ac);
-          uint32_t b1 = *reinterpret_cast<const uint32_t*>(ws + bn * RL_LD + k0 + ac + 8);
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(ws + bn * RL_LD + k0 + ac);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(ws + bn * RL_LD + k0 + ac + 8);
           asm volatile(
               "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
               "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -92,7 +107,11 @@ __global__ void __launch_bounds__(128) router_logits_bf16(RouterLogitsParams p, 
         }
       }
     }
+    const int nc = c + RL_STAGES - 1;
+    if (nc < nchunks) load_chunk(nc);
+    cp_async_commit();
   }
+  cp_async_wait<0>();
   // C fragment: c0,c1 -> (row lane/4, cols 2*(lane%4)+{0,1}); c2,c3 -> row + 8.
   const int r0 = tok0 + warp * 16 + (lane >> 2);
 #pragma unroll
@@ -485,8 +504,25 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
     int cols = RL_MAXNT * 8;
     while (cols > 8 && tok_blocks * ((p.E1 + cols - 1) / cols) < 2 * num_sms()) cols -= 8;
     dim3 grid(tok_blocks, (p.E1 + cols - 1) / cols);
-    const size_t smem = static_cast<size_t>(RL_TOK + cols) * RL_LD * sizeof(__nv_bfloat16);
-    launch_kernel(router_logits_bf16, grid, dim3(128), smem, stream, p, cols);
+    const size_t stage_bytes = static_cast<size_t>(RL_TOK + cols) * RL_LD * sizeof(__nv_bfloat16);
+    static uint64_t attr_set_mask = 0;  // one bit per device ordinal
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_set_mask & bit)) {
+      const int max4 = 4 * (RL_TOK + RL_MAXNT * 8) * RL_LD * sizeof(__nv_bfloat16);
+      const int max8 = 8 * (RL_TOK + 24) * RL_LD * sizeof(__nv_bfloat16);
+      if (cudaFuncSetAttribute(router_logits_bf16<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max4) !=
+              cudaSuccess ||
+          cudaFuncSetAttribute(router_logits_bf16<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max8) !=
+              cudaSuccess)
+        return -3;
+      attr_set_mask |= bit;
+    }
+    if (cols <= 24)
+      launch_kernel(router_logits_bf16<8>, grid, dim3(128), 8 * stage_bytes, stream, p, cols);
+    else
+      launch_kernel(router_logits_bf16<4>, grid, dim3(128), 4 * stage_bytes, stream, p, cols);
   } else {
     const int grid = (p.T * 32 + 255) / 256;
     launch_kernel(router_logits_f32, dim3(grid), dim3(256), 0, stream, p);

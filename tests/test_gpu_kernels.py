@@ -214,10 +214,11 @@ def test_grouped_down_row_scatter(cuda_device, variant, monkeypatch):
     assert max_rel(y, expect) < TIGHT_TOL
 
 
+@pytest.mark.parametrize("K", [1, 2, 3, 6, 8])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_combine_matches_fp32_reference(cuda_device, dtype):
-    g = torch.Generator().manual_seed(11)
-    T, K, H = 77, 6, 384
+def test_combine_matches_fp32_reference(cuda_device, dtype, K):
+    g = torch.Generator().manual_seed(11 + K)
+    T, H = 77, 384
     y = torch.randn(T * K, H, generator=g).to(dtype)
     pos = torch.randperm(T * K, generator=g).view(T, K).to(torch.int32)
     w = torch.rand(T, K, generator=g)
