@@ -15,7 +15,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libb200moe.so")
-SOURCES = ["router.cu", "permute.cu", "norm.cu", "grouped_gemm.cu", "grouped_gemm_wm.cu", "grouped_gemm_f32.cu", "ep_nvlink.cu", "capi.cu"]
+SOURCES = ["router.cu", "permute.cu", "norm.cu", "grouped_gemm.cu", "grouped_gemm_wm.cu", "grouped_gemm_2sm.cu", "grouped_gemm_f32.cu", "ep_nvlink.cu", "capi.cu"]
 HEADERS = ["ptx.cuh", "common.cuh", "kernels.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -378,11 +378,20 @@ static bool decode_regime(const GemmLaunch& L) {
   return rows <= 48 * static_cast<int64_t>(L.p.P);
 }
 
+// Prefill regime with full 256-row pair tiles on average: the CTA-pair kernel
+// (grouped_gemm_2sm.cu), which stages a third fewer shared-memory bytes per FLOP.
+static bool pair_regime(const GemmLaunch& L) {
+  const int64_t rows = L.rows_hint > 0 ? L.rows_hint : L.rows_cap;
+  return rows >= 256 * static_cast<int64_t>(L.p.P);
+}
+
 int launch_grouped_swiglu(const GemmLaunch& L, cudaStream_t stream) {
   if (L.p.P > GM_MAXP) return -4;
   const int v = L.variant;
   if (v == kGemmWeightMajor || (v == kGemmAuto && decode_regime(L))) return launch_grouped_wm(L, true, stream);
   if (v == kGemmTokenMajorSmallM) return run_gemm<64, 9, true, 32>(L, stream);
+  if ((v == kGemmTokenMajorPair || (v == kGemmAuto && pair_regime(L))) && pair_gemm_supported(L, true))
+    return launch_grouped_pair(L, true, stream);
   return run_gemm<256, 4, true, GM_BM>(L, stream);
 }
 
@@ -391,6 +400,8 @@ int launch_grouped_down(const GemmLaunch& L, cudaStream_t stream) {
   const int v = L.variant;
   if (v == kGemmWeightMajor || (v == kGemmAuto && decode_regime(L))) return launch_grouped_wm(L, false, stream);
   if (v == kGemmTokenMajorSmallM) return run_gemm<64, 9, false, 32>(L, stream);
+  if ((v == kGemmTokenMajorPair || (v == kGemmAuto && pair_regime(L))) && pair_gemm_supported(L, false))
+    return launch_grouped_pair(L, false, stream);
   return run_gemm<256, 4, false, GM_BM>(L, stream);
 }
 

@@ -268,6 +268,7 @@ enum GemmVariant : int {
   kGemmTokenMajor = 1,        // M = 128 token rows x N = 256 weight rows (prefill)
   kGemmTokenMajorSmallM = 2,  // 32 token rows per tile, N = 64
   kGemmWeightMajor = 3,       // M = 128 weight rows x N = 32 tokens (decode)
+  kGemmTokenMajorPair = 4,    // CTA pairs: M = 256 token rows x N = 256 (cta_group::2)
 };
 
 struct GemmLaunch {
@@ -285,6 +286,8 @@ struct GemmLaunch {
 int make_tma_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
                     int box_rows);
 int launch_grouped_wm(const GemmLaunch& L, bool swiglu, cudaStream_t stream);
+bool pair_gemm_supported(const GemmLaunch& L, bool swiglu);
+int launch_grouped_pair(const GemmLaunch& L, bool swiglu, cudaStream_t stream);
 
 struct GemmF32Params {
   const float* a;          // [rows, K]

@@ -188,7 +188,8 @@ class MoELayer:
         if offs is None:
             offs = torch.tensor([0, T], dtype=torch.int32, device=self.device)
             self._shared_offsets[T] = offs
-        act = ops.grouped_swiglu(x, offs, self.p.shared_gate_up[None], status=self.status)
+        act = ops.grouped_swiglu(x, offs, self.p.shared_gate_up[None], status=self.status,
+                                 hook_name="shared_swiglu")
         st.shared_out = ops.grouped_down(act, offs, self.p.shared_down[None], status=self.status)
 
     # ------------------------------------------------------------ MOE

@@ -247,9 +247,11 @@ def permute(x: torch.Tensor, r: RouterOutput, *, num_slots: int, E1: int,
 
 def grouped_swiglu(x: torch.Tensor, expert_offsets: torch.Tensor, w_gate_up: torch.Tensor,
                    *, out: Optional[torch.Tensor] = None,
-                   status: Optional[torch.Tensor] = None, rows_hint: int = 0) -> torch.Tensor:
+                   status: Optional[torch.Tensor] = None, rows_hint: int = 0,
+                   hook_name: str = "grouped_swiglu") -> torch.Tensor:
     """act = silu(x Wg^T) * (x Wu^T) per expert segment; x [rows, H] bf16 expert-major.
-    rows_hint: expected rows when x is a worst-case buffer (picks the kernel)."""
+    rows_hint: expected rows when x is a worst-case buffer (picks the kernel);
+    hook_name: the name EVENT_HOOK sees (the shared expert reports itself apart)."""
     _need_cuda(x, expert_offsets, w_gate_up, status)
     if x.dtype != w_gate_up.dtype or x.dtype not in (torch.bfloat16, torch.float32):
         raise TypeError("grouped GEMMs take bfloat16 (tensor cores) or float32 activations and weights")
@@ -266,11 +268,11 @@ def grouped_swiglu(x: torch.Tensor, expert_offsets: torch.Tensor, w_gate_up: tor
                   P, H, I, w_gate_up.data_ptr(), act.data_ptr(), act.stride(0), _stream())
         _count(1 if x.shape[0] else 0)
         return act
-    _hook("grouped_swiglu", "start")
+    _hook(hook_name, "start")
     _lib.call("b200moe_grouped_swiglu_ex", x.data_ptr(), x.stride(0), x.shape[0], rows_hint,
               offs.data_ptr(), P, H, I, w_gate_up.data_ptr(), act.data_ptr(), act.stride(0),
               _ptr(status), _stream())
-    _hook("grouped_swiglu", "end")
+    _hook(hook_name, "end")
     _count(1 if x.shape[0] else 0)
     return act
 

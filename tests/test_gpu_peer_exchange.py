@@ -179,3 +179,29 @@ def test_wait_that_runs_out_reports_timeout(cuda_device):
     finally:
         for xg in xgs:
             xg.close()
+
+
+@pytest.mark.parametrize("variant", ["token", "pair"])
+@pytest.mark.parametrize("name", ["mixtral_g2", "dsv2_g2"])
+def test_peer_exchange_with_prefill_gemm_kernels(cuda_device, name, variant, monkeypatch):
+    """The fused exchange through the prefill GEMM kernels (single-CTA and CTA-pair),
+    whose epilogues store the down-projection rows straight into the senders'
+    combine regions; both paths run the same forced kernel."""
+    monkeypatch.setenv("B200MOE_GEMM_VARIANT", variant)
+    case = cases.CASES[name]
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    shape, layers = _layers(case, cuda_device, status)
+    T = case["T"]
+    xs = [C.hidden_states(shape, T, rank=r).to(cuda_device) for r in range(case["G"])]
+    ref = _nccl_path(layers, xs)
+    xgs = _attach(layers, shape, T, cuda_device, status, True)
+    try:
+        for _ in range(2):
+            outs = forward_peer_single_device(layers, xs)
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0
+            for r in range(case["G"]):
+                assert torch.equal(outs[r], ref[r]), (name, variant, r)
+    finally:
+        for xg in xgs:
+            xg.close()
