@@ -326,6 +326,14 @@ def run_ours(args):
         launches = launches_per_step * args.steps if launches_per_step is not None else ops.LAUNCHES["count"]
         barrier()
         clocks = sampler.stop() if sampler else None
+        if world > 1 and with_roofline:
+            # every rank's median SM clock: under the power cap GPUs settle at different
+            # clocks, and the slowest one paces every exchange
+            mine = torch.tensor([clocks["sm_mhz"] if clocks else -1.0], dtype=torch.float64, device=device)
+            allc = torch.empty(world, dtype=torch.float64, device=device)
+            dist.all_gather_into_tensor(allc, mine)
+            if clocks is not None:
+                clocks = dict(clocks, sm_mhz_per_rank=[round(v, 1) for v in allc.tolist()])
         ms = t0.elapsed_time(t1) / args.steps
         ms = max_over_ranks(ms)
         kernel_ms = []

@@ -25,6 +25,7 @@ G > 1 there are two transports:
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import List, Optional
 
@@ -105,6 +106,9 @@ class MoELayer:
                  n_group: int = 1, topk_group: int = 1, exchange=None):
         self.p = params
         self.exchange = exchange  # PeerExchange: the NVLink transport for G > 1
+        # shared expert on a second stream at decode sizes (G == 1); B200MOE_OVERLAP_SHARED=0 off
+        self.overlap_shared = os.environ.get("B200MOE_OVERLAP_SHARED", "1") != "0"
+        self._side = None
         self.placement = placement
         self.top_k = top_k
         self.norm_topk_prob = norm_topk_prob
@@ -236,6 +240,34 @@ class MoELayer:
                                      residual_out=residual_out, normed=nbuf)
         return ro, self.forward(normed, out=out)
 
+    # ------------------------------------------------------------ one rank
+    def _overlap(self, T: int) -> bool:
+        """Run the shared expert on a second stream, beside the routing chain?  Only
+        for decode-sized batches: there both are latency- or HBM-bound short kernels;
+        at prefill both are persistent tensor-core GEMMs that would only compete."""
+        return (self.overlap_shared and self.p.shared_gate_up is not None
+                and T * self.top_k <= 48 * self.P)
+
+    def _forward_local(self, x: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
+        if not self._overlap(x.shape[0]):
+            st = self.route_and_permute(x)
+            self.shared_expert(x, st)
+            return self.unpermute(st, self.experts_local(st), out)
+        cur = torch.cuda.current_stream(self.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        side = self._side
+        side.wait_stream(cur)                       # x is ready
+        held = DispatchState(T=x.shape[0], route=None, perm=None)
+        with torch.cuda.stream(side):
+            self.shared_expert(x, held)
+        st = self.route_and_permute(x)
+        y = self.experts_local(st)
+        cur.wait_stream(side)                       # join before the combine reads it
+        held.shared_out.record_stream(cur)
+        st.shared_out = held.shared_out
+        return self.unpermute(st, y, out)
+
     # ------------------------------------------------------------ NVLink transport
     def _fused(self) -> bool:
         # the fused forms run the bf16 tensor-core kernels; fp32 layers use the plain ones
@@ -287,11 +319,10 @@ class MoELayer:
         """Routed output plus the (gated) shared-expert output for this rank's tokens."""
         if self.G > 1 and self.exchange is not None:
             return self.forward_peer(x, out)
+        if self.G == 1:
+            return self._forward_local(x, out)
         st = self.route_and_permute(x)
         self.shared_expert(x, st)
-        if self.G == 1:
-            y = self.experts_local(st)
-            return self.unpermute(st, y, out)
         counts = self.exchange_counts(st)
         self.plan_exchange(st, counts)
         self.dispatch(st)

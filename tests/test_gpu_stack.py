@@ -36,3 +36,11 @@ def test_graph_replay_equals_eager(cuda_device, cfg, T):
         torch.cuda.synchronize()
         assert torch.equal(eager, replay)
         assert torch.isfinite(replay.float()).all()
+        # the shared expert on its own stream (decode sizes) changes no bit
+        for l in layers:
+            l.overlap_shared = False
+        serial = stack.forward(x).clone()
+        for l in layers:
+            l.overlap_shared = True
+        torch.cuda.synchronize()
+        assert torch.equal(serial, eager)
