@@ -291,7 +291,9 @@ class MoELayer:
         Plain: the down GEMM writes back into the receive region (arrival order) and a
         combine-send kernel returns the rows."""
         xg = self.exchange
-        hint = st.T * self.top_k
+        # expected rows per rank (every rank routes a similar batch); a rank without
+        # tokens of its own still receives rows from the others
+        hint = max(st.T, 1) * self.top_k
         fused = self._fused()
         xe, row_map, offs = xg.collect(rows_hint=hint, peer_rows=fused)
         act = ops.grouped_swiglu(xe, offs, self.p.w_gate_up, out=xg.act, status=self.status, rows_hint=hint)
