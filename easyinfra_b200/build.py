@@ -16,7 +16,7 @@ REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libb200moe.so")
 SOURCES = ["router.cu", "permute.cu", "norm.cu", "grouped_gemm.cu", "grouped_gemm_wm.cu", "grouped_gemm_2sm.cu", "grouped_gemm_f32.cu", "ep_nvlink.cu", "capi.cu"]
-HEADERS = ["ptx.cuh", "common.cuh", "kernels.cuh"]
+HEADERS = ["ptx.cuh", "common.cuh", "kernels.cuh", "norm_row.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -153,7 +153,9 @@ int select_common(const float* logits, int has_shared_gate, int T, int E, int K,
                   int max_rep, int num_slots, int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
                   float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets,
                   const RouterWs& ws, int* status, cudaStream_t stream, int scoring = 0,
-                  int n_group = 1, int topk_group = 1, const float* correction_bias = nullptr) {
+                  int n_group = 1, int topk_group = 1, const float* correction_bias = nullptr,
+                  const RouterLogitsParams* fuse_lp = nullptr, const AddNormParams* fuse_np = nullptr,
+                  int x_dtype = 0) {
   RouterSelectParams s;
   s.scoring = scoring;
   s.n_group = n_group;
@@ -183,6 +185,12 @@ int select_common(const float* logits, int has_shared_gate, int T, int E, int K,
   s.slot_offsets = slot_offsets;
   s.ticket = ws.ticket;
   s.status = status;
+  if (fuse_lp != nullptr) {
+    // logits (and the prologue) fused with the selection: one launch for small batches
+    if (launch_router_small_fused(*fuse_lp, s, fuse_np, x_dtype, stream))
+      return fail(B200MOE_ECUDA, "router_small_fused: %s", cudaGetErrorString(cudaGetLastError()));
+    return check_launch("router_small_fused");
+  }
   launch_router_select(s, stream);
   return check_launch("router_select");
 }
@@ -264,12 +272,78 @@ int b200moe_router(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
   lp.H = H;
   lp.E1 = E1;
   lp.logits = logits_out ? logits_out : ws.logits;
-  if (launch_router_logits(lp, x_dtype, st)) return fail(B200MOE_ECUDA, "router_logits: kernel setup failed");
-  if ((rc = check_launch("router_logits"))) return rc;
+  const bool fuse = router_small_fused_ok(T, H, x_dtype, num_slots, 0, false);
+  if (!fuse) {
+    if (launch_router_logits(lp, x_dtype, st)) return fail(B200MOE_ECUDA, "router_logits: kernel setup failed");
+    if ((rc = check_launch("router_logits"))) return rc;
+  }
   return select_common(lp.logits, has_shared_gate, T, E, K, renorm, scale,
                        x_dtype == B200MOE_DTYPE_BF16, log2phy, rep_count, max_rep, num_slots,
                        topk_ids, topk_w, phys_ids, shared_gate, slot_counts, slot_offsets, ws,
-                       status, st);
+                       status, st, 0, 1, 1, nullptr, fuse ? &lp : nullptr, nullptr, x_dtype);
+}
+
+int b200moe_add_rmsnorm_router(const void* residual, const void* hidden, const void* norm_weight, float eps,
+                               int64_t ld, void* residual_out, void* normed, int64_t ld_normed, int x_dtype,
+                               const void* gate_w, const float* gate_bias, int has_shared_gate, int T, int H, int E,
+                               int K, int renorm, float scale, const int32_t* log2phy, const int32_t* rep_count,
+                               int max_rep, int num_slots, int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                               float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets, float* logits_out,
+                               void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  if (x_dtype != B200MOE_DTYPE_BF16 && x_dtype != B200MOE_DTYPE_F32)
+    return fail(B200MOE_EUNSUPPORTED, "x_dtype=%d", x_dtype);
+  const int eb = dtype_bytes(x_dtype);
+  if (T > 0 && (!residual || !norm_weight || !residual_out || !normed))
+    return fail(B200MOE_EINVAL, "null prologue pointer");
+  if (T > 0 && (!aligned16(residual) || !aligned16(residual_out) || !aligned16(normed) ||
+                (hidden && !aligned16(hidden)) || !aligned16(norm_weight) || (ld * eb) % 16 != 0 ||
+                (ld_normed * eb) % 16 != 0 || ld < H || ld_normed < H))
+    return fail(B200MOE_EINVAL, "prologue rows must be 16-byte aligned with 16-byte strides");
+  const bool fuse = router_small_fused_ok(T, H, x_dtype, num_slots, 0, true);
+  if (!fuse) {
+    // larger batches: the prologue kernel, then the router on its output
+    if ((rc = b200moe_add_rmsnorm(residual, hidden, norm_weight, eps, T, H, x_dtype, ld, residual_out, normed,
+                                  ld_normed, stream)))
+      return rc;
+    return b200moe_router(normed, ld_normed, x_dtype, gate_w, gate_bias, has_shared_gate, T, H, E, K, renorm, scale,
+                          log2phy, rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate,
+                          slot_counts, slot_offsets, logits_out, workspace, workspace_bytes, status, stream);
+  }
+  rc = check_select_args(T, E, K, num_slots, log2phy, rep_count, max_rep, topk_ids, topk_w, phys_ids, slot_counts,
+                         slot_offsets, has_shared_gate, shared_gate);
+  if (rc) return rc;
+  if (!gate_w || !workspace || !aligned16(gate_w)) return fail(B200MOE_EINVAL, "null or misaligned gate_w / workspace");
+  const int E1 = E + (has_shared_gate ? 1 : 0);
+  const RouterWs ws = router_ws_layout(workspace, T, E1, num_slots);
+  if (workspace_bytes < ws.bytes)
+    return fail(B200MOE_EINVAL, "workspace too small: %zu < %zu", workspace_bytes, ws.bytes);
+  AddNormParams np;
+  np.residual = residual;
+  np.hidden = hidden;
+  np.weight = norm_weight;
+  np.eps = eps;
+  np.T = T;
+  np.H = H;
+  np.dtype = x_dtype;
+  np.ld = ld;
+  np.residual_out = residual_out;
+  np.normed = normed;
+  np.ld_normed = ld_normed;
+  RouterLogitsParams lp;
+  lp.x = normed;
+  lp.ldx = ld_normed;
+  lp.w = gate_w;
+  lp.bias = gate_bias;
+  lp.T = T;
+  lp.H = H;
+  lp.E1 = E1;
+  lp.logits = logits_out ? logits_out : ws.logits;
+  return select_common(lp.logits, has_shared_gate, T, E, K, renorm, scale, x_dtype == B200MOE_DTYPE_BF16, log2phy,
+                       rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate, slot_counts,
+                       slot_offsets, ws, status, static_cast<cudaStream_t>(stream), 0, 1, 1, nullptr, &lp, &np,
+                       x_dtype);
 }
 
 int b200moe_router_sigmoid_grouped(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
@@ -308,11 +382,15 @@ int b200moe_router_sigmoid_grouped(const void* x, int64_t ldx, int x_dtype, cons
   lp.E1 = E;
   lp.logits = logits_out ? logits_out : ws.logits;
   lp.round_bf16 = 0;  // the reference computes these logits in fp32
-  if (launch_router_logits(lp, x_dtype, st)) return fail(B200MOE_ECUDA, "router_logits: kernel setup failed");
-  if ((rc = check_launch("router_logits"))) return rc;
+  const bool fuse = router_small_fused_ok(T, H, x_dtype, num_slots, 1, false);
+  if (!fuse) {
+    if (launch_router_logits(lp, x_dtype, st)) return fail(B200MOE_ECUDA, "router_logits: kernel setup failed");
+    if ((rc = check_launch("router_logits"))) return rc;
+  }
   return select_common(lp.logits, 0, T, E, K, renorm && K > 1, scale, x_dtype == B200MOE_DTYPE_BF16,
                        log2phy, rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, nullptr,
-                       slot_counts, slot_offsets, ws, status, st, 1, n_group, topk_group, correction_bias);
+                       slot_counts, slot_offsets, ws, status, st, 1, n_group, topk_group, correction_bias,
+                       fuse ? &lp : nullptr, nullptr, x_dtype);
 }
 
 int b200moe_router_from_logits(const float* logits, int has_shared_gate, int T, int E, int K,

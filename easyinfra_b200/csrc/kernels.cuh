@@ -310,6 +310,11 @@ int launch_ep_combine_send(const EpParams& p, const void* y_recv, int64_t max_ro
 int launch_ep_wait_comb(const EpParams& p, uint32_t* expect, uint64_t timeout_ns, cudaStream_t stream);
 
 int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t stream);
+// Small batches (T <= 8): logits, selection and optionally the block prologue in one
+// launch (router.cu).  sp must describe one token block (nblocks 1).
+bool router_small_fused_ok(int T, int H, int x_dtype, int num_slots, int scoring, bool has_norm);
+int launch_router_small_fused(const RouterLogitsParams& lp, const RouterSelectParams& sp, const AddNormParams* np,
+                              int x_dtype, cudaStream_t stream);
 int launch_grouped_gemm_f32(const GemmF32Params& p, bool swiglu, cudaStream_t stream);
 int launch_router_select(const RouterSelectParams& p, cudaStream_t stream);
 int launch_permute(const PermuteParams& p, cudaStream_t stream);

@@ -9,91 +9,21 @@
 // the normalisation runs in fp32 and is rounded before the weight multiply, whose
 // product is rounded again.  One CTA per token; the row is read once from HBM and
 // kept in registers for the second pass.
-#include "kernels.cuh"
+#include "norm_row.cuh"
 
 namespace b200moe {
 
+// One CTA per token; the row is read once from HBM and kept in registers for the
+// second pass (add_rmsnorm_row, norm_row.cuh).
 template <typename E>
-__device__ __forceinline__ float to_f(E v);
-template <>
-__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
-template <>
-__device__ __forceinline__ float to_f<float>(float v) { return v; }
-
-template <typename E>
-__device__ __forceinline__ E from_f(float v);
-template <>
-__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
-template <>
-__device__ __forceinline__ float from_f<float>(float v) { return v; }
-
-// One CTA per token: each thread holds up to NORM_MAXV 16-byte vectors of the row in
-// registers between the two passes; the sum of squares is reduced across the CTA.
-constexpr int NORM_THREADS = 256;
-constexpr int NORM_MAXV = 8;   // rows up to 256 * 8 * 16 B = 32 KB (H <= 16384 bf16)
-
-template <typename E>
-__global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(AddNormParams p) {
+__global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(const __grid_constant__ AddNormParams p) {
   __shared__ float red[NORM_THREADS / 32];
   pdl_trigger();
   pdl_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x;
-  const E* res = static_cast<const E*>(p.residual) + t * p.ld;
-  const E* hid = p.hidden ? static_cast<const E*>(p.hidden) + t * p.ld : nullptr;
   E* rout = static_cast<E*>(p.residual_out) + t * p.ld;
-  constexpr int V = 16 / sizeof(E);  // elements per 16-byte vector
-  const int nvec = p.H / V;
-  uint4 keep[NORM_MAXV];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < NORM_MAXV; ++i) {
-    const int vi = threadIdx.x + i * NORM_THREADS;
-    if (vi < nvec) {
-      const uint4 a = *reinterpret_cast<const uint4*>(res + vi * V);
-      uint4 o = a;
-      E* oe = reinterpret_cast<E*>(&o);
-      if (hid) {
-        const uint4 b = *reinterpret_cast<const uint4*>(hid + vi * V);
-        const E* ae = reinterpret_cast<const E*>(&a);
-        const E* be = reinterpret_cast<const E*>(&b);
-#pragma unroll
-        for (int j = 0; j < V; ++j) oe[j] = from_f<E>(to_f<E>(ae[j]) + to_f<E>(be[j]));
-      }
-#pragma unroll
-      for (int j = 0; j < V; ++j) {
-        const float f = to_f<E>(oe[j]);
-        ss = fmaf(f, f, ss);
-      }
-      *reinterpret_cast<uint4*>(rout + vi * V) = o;
-      keep[i] = o;
-    }
-  }
-  if (p.normed == nullptr) return;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int q = 0; q < NORM_THREADS / 32; ++q) tot += red[q];
-  const float inv = rsqrtf(tot / static_cast<float>(p.H) + p.eps);
-  const E* w = static_cast<const E*>(p.weight);
-  E* nout = static_cast<E*>(p.normed) + t * p.ld_normed;
-#pragma unroll
-  for (int i = 0; i < NORM_MAXV; ++i) {
-    const int vi = threadIdx.x + i * NORM_THREADS;
-    if (vi < nvec) {
-      const uint4 wv = *reinterpret_cast<const uint4*>(w + vi * V);
-      const E* ae = reinterpret_cast<const E*>(&keep[i]);
-      const E* we = reinterpret_cast<const E*>(&wv);
-      uint4 o;
-      E* oe = reinterpret_cast<E*>(&o);
-#pragma unroll
-      for (int j = 0; j < V; ++j) oe[j] = from_f<E>(to_f<E>(we[j]) * to_f<E>(from_f<E>(to_f<E>(ae[j]) * inv)));
-      *reinterpret_cast<uint4*>(nout + vi * V) = o;
-    }
-  }
+  E* nout = p.normed ? static_cast<E*>(p.normed) + t * p.ld_normed : nullptr;
+  add_rmsnorm_row<E>(p, t, rout, nout, nullptr, red);
 }
 
 int launch_add_rmsnorm(const AddNormParams& p, cudaStream_t stream) {

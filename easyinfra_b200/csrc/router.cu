@@ -20,6 +20,7 @@
 //                       finish turns the histograms into slot counts, slot offsets
 //                       and per-(slot, block) write offsets for the permute kernel.
 #include "kernels.cuh"
+#include "norm_row.cuh"
 
 namespace b200moe {
 
@@ -226,18 +227,13 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
   return va > vb || (va == vb && ia < ib);
 }
 
-__global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
-  extern __shared__ int32_t hist[];  // [num_slots], then (scoring 1) 8 warps x 256 floats
-  __shared__ int s_last;
-  pdl_trigger();
-  pdl_wait();
+// One warp per token of [t_begin, t_end): selection, weights, replica pick and the
+// CTA's slot histogram (hist, shared, zeroed by the caller; the scoring-1 scratch
+// follows it).  Shared by router_select and the fused small-batch router.
+__device__ __forceinline__ void select_tokens(const RouterSelectParams& p, int t_begin, int t_end,
+                                              int32_t* hist) {
   float* cbuf = reinterpret_cast<float*>(hist + p.num_slots) + (threadIdx.x >> 5) * 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) hist[s] = 0;
-  __syncthreads();
-
-  const int t_begin = blockIdx.x * p.tb;
-  const int t_end = min(p.T, t_begin + p.tb);
   for (int t = t_begin + warp; t < t_end; t += blockDim.x >> 5) {
     const float* lg = p.logits + static_cast<int64_t>(t) * p.E1;
     float v[RS_MAXJ];     // selection key per owned expert
@@ -384,15 +380,13 @@ __global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
       p.shared_gate[t] = 1.f / (1.f + expf(-g));
     }
   }
-  __syncthreads();
-  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x)
-    p.block_counts[static_cast<int64_t>(s) * p.nblocks + blockIdx.x] = hist[s];
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(p.ticket, 1u) == static_cast<uint32_t>(p.nblocks - 1));
-  __syncthreads();
-  if (!s_last) return;
+}
 
+// Run by every thread of the CTA that arrived last, once every CTA's histogram is in
+// block_counts: slot totals, slot offsets, absolute per-(slot, block) offsets; resets
+// the ticket.  hist is shared scratch of num_slots ints.
+__device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32_t* hist) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // ---- last CTA: slot totals, slot offsets, absolute per-(slot, block) offsets.
   __threadfence();
   const int nb = p.nblocks;
@@ -485,6 +479,163 @@ __global__ void __launch_bounds__(256) router_select(RouterSelectParams p) {
     }
   }
   if (threadIdx.x == 0) *p.ticket = 0u;
+}
+
+__global__ void __launch_bounds__(256) router_select(const __grid_constant__ RouterSelectParams p) {
+  extern __shared__ int32_t hist[];  // [num_slots], then (scoring 1) 8 warps x 256 floats
+  __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
+  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) hist[s] = 0;
+  __syncthreads();
+  const int t_begin = blockIdx.x * p.tb;
+  select_tokens(p, t_begin, min(p.T, t_begin + p.tb), hist);
+  __syncthreads();
+  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x)
+    p.block_counts[static_cast<int64_t>(s) * p.nblocks + blockIdx.x] = hist[s];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(p.ticket, 1u) == static_cast<uint32_t>(p.nblocks - 1));
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  select_finish(p, hist);
+}
+
+// ------------------------------------------------------------------ fused small batch
+// T <= RG tokens (decode): one CTA per router column computes that column's logits for
+// every token — the GEMV of router_logits_gemv with the same thread mapping and
+// reduction order, on token rows staged in shared memory — and the CTA that finishes
+// last runs the selection for all tokens (select_tokens / select_finish, one token
+// block).  With the block prologue fused in (has_norm), every CTA first builds the
+// normed rows itself with add_rmsnorm_row (CTA 0 also writes residual_out and
+// normed).  One launch replaces two (router) or three (prologue + router); the bits
+// are those of the separate kernels.
+constexpr size_t kFusedSmemMax = 160 * 1024;
+
+template <typename E>
+__global__ void __launch_bounds__(256) router_small_fused(const __grid_constant__ RouterLogitsParams lp,
+                                                          const __grid_constant__ RouterSelectParams sp,
+                                                          const __grid_constant__ AddNormParams np, int has_norm) {
+  extern __shared__ __align__(16) uint8_t dyn[];
+  __shared__ float red[8][RG];
+  __shared__ float nred[NORM_THREADS / 32];
+  __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x;
+  const int T = lp.T, H = lp.H;
+  constexpr int V = 16 / sizeof(E);
+  E* xs = reinterpret_cast<E*>(dyn);  // [T][H]
+  int32_t* hist = reinterpret_cast<int32_t*>(dyn + ((static_cast<size_t>(T) * H * sizeof(E) + 15) & ~size_t(15)));
+
+  if (has_norm) {
+    for (int t = 0; t < T; ++t) {
+      E* rout = (e == 0) ? static_cast<E*>(np.residual_out) + static_cast<int64_t>(t) * np.ld : nullptr;
+      E* ng = (e == 0 && np.normed) ? static_cast<E*>(np.normed) + static_cast<int64_t>(t) * np.ld_normed : nullptr;
+      add_rmsnorm_row<E>(np, t, rout, xs + static_cast<int64_t>(t) * H, ng, nred);
+    }
+  } else {
+    const E* x = static_cast<const E*>(lp.x);
+    const int vpr = H / V;
+    for (int i = threadIdx.x; i < T * vpr; i += blockDim.x) {
+      const int t = i / vpr, c = (i - t * vpr) * V;
+      *reinterpret_cast<uint4*>(xs + static_cast<int64_t>(t) * H + c) =
+          __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * lp.ldx + c));
+    }
+  }
+  __syncthreads();
+
+  const E* w = static_cast<const E*>(lp.w) + static_cast<int64_t>(e) * H;
+  float acc[RG];
+#pragma unroll
+  for (int i = 0; i < RG; ++i) acc[i] = 0.f;
+  for (int c = threadIdx.x * V; c < H; c += 256 * V) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + c));
+    const E* we = reinterpret_cast<const E*>(&wv);
+#pragma unroll
+    for (int i = 0; i < RG; ++i) {
+      if (i < T) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(i) * H + c);
+        const E* xe = reinterpret_cast<const E*>(&xv);
+#pragma unroll
+        for (int j = 0; j < V; ++j) acc[i] = fmaf(static_cast<float>(xe[j]), static_cast<float>(we[j]), acc[i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RG; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < RG; ++i) red[warp][i] = acc[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < T) {
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v += red[q][threadIdx.x];
+    if (lp.bias) v += lp.bias[e];
+    if (sizeof(E) == 2 && lp.round_bf16) v = bf16_round(v);
+    lp.logits[static_cast<int64_t>(threadIdx.x) * lp.E1 + e] = v;
+  }
+
+  // the last column to finish selects for every token
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(sp.ticket, 1u) == gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int s = threadIdx.x; s < sp.num_slots; s += blockDim.x) hist[s] = 0;
+  __syncthreads();
+  select_tokens(sp, 0, T, hist);
+  __syncthreads();
+  for (int s = threadIdx.x; s < sp.num_slots; s += blockDim.x) sp.block_counts[s] = hist[s];  // one block
+  __threadfence();
+  __syncthreads();
+  select_finish(sp, hist);
+}
+
+size_t router_small_fused_smem(int T, int H, int x_dtype, int num_slots, int scoring) {
+  const size_t rows = (static_cast<size_t>(T) * H * dtype_bytes(x_dtype) + 15) & ~size_t(15);
+  return rows + static_cast<size_t>(num_slots) * sizeof(int32_t) + (scoring == 1 ? 8 * 256 * sizeof(float) : 0);
+}
+
+bool router_small_fused_ok(int T, int H, int x_dtype, int num_slots, int scoring, bool has_norm) {
+  const int V = 16 / dtype_bytes(x_dtype);
+  if (T < 1 || T > RG || H % V != 0) return false;
+  if (has_norm && H / V > NORM_THREADS * NORM_MAXV) return false;
+  return router_small_fused_smem(T, H, x_dtype, num_slots, scoring) <= kFusedSmemMax;
+}
+
+int launch_router_small_fused(const RouterLogitsParams& lp, const RouterSelectParams& sp, const AddNormParams* np,
+                              int x_dtype, cudaStream_t stream) {
+  static uint64_t attr_set_mask = 0;  // one bit per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set_mask & bit)) {
+    if (cudaFuncSetAttribute(router_small_fused<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kFusedSmemMax)) != cudaSuccess ||
+        cudaFuncSetAttribute(router_small_fused<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kFusedSmemMax)) != cudaSuccess)
+      return -3;
+    attr_set_mask |= bit;
+  }
+  AddNormParams none{};
+  const size_t smem = router_small_fused_smem(lp.T, lp.H, x_dtype, sp.num_slots, sp.scoring);
+  cudaError_t e;
+  if (x_dtype == kDtypeBF16)
+    e = launch_kernel(router_small_fused<__nv_bfloat16>, dim3(lp.E1), dim3(256), smem, stream, lp, sp,
+                      np ? *np : none, np ? 1 : 0);
+  else
+    e = launch_kernel(router_small_fused<float>, dim3(lp.E1), dim3(256), smem, stream, lp, sp, np ? *np : none,
+                      np ? 1 : 0);
+  return e == cudaSuccess ? 0 : -2;
 }
 
 // ------------------------------------------------------------------ host launchers

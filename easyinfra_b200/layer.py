@@ -139,7 +139,9 @@ class MoELayer:
             raise ValueError("gate_w rows must be E (+1 with a shared-expert gate)")
 
     # ------------------------------------------------------------ ROUTING_DISPATCH
-    def route(self, x: torch.Tensor) -> ops.RouterOutput:
+    def route(self, x: torch.Tensor, pre: Optional[ops.RouterOutput] = None) -> ops.RouterOutput:
+        if pre is not None:  # already routed (fused with the block prologue)
+            return pre
         l2p = self.log2phy if self.use_map else None
         rep = self.rep_count if self.use_map else None
         if self.scoring == "sigmoid_grouped":
@@ -155,9 +157,9 @@ class MoELayer:
                            num_slots=self.G * self.P, workspace=self.ws, status=self.status)
         return r
 
-    def route_and_permute(self, x: torch.Tensor) -> DispatchState:
+    def route_and_permute(self, x: torch.Tensor, pre: Optional[ops.RouterOutput] = None) -> DispatchState:
         """Router + permute into a local send buffer (no exchange)."""
-        r = self.route(x)
+        r = self.route(x, pre)
         perm = ops.permute(x, r, num_slots=self.G * self.P, E1=self.p.gate_w.shape[0])
         return DispatchState(T=x.shape[0], route=r, perm=perm)
 
@@ -236,6 +238,17 @@ class MoELayer:
         nbuf = self._normed.get(key)
         if nbuf is None:
             nbuf = self._normed[key] = torch.empty_like(residual)
+        if self.scoring == "softmax" and residual.shape[0] <= 8:
+            # decode-sized batch: prologue, logits and selection in one launch
+            l2p = self.log2phy if self.use_map else None
+            rep = self.rep_count if self.use_map else None
+            ro, normed, r = ops.add_rmsnorm_router(
+                residual, hidden, self.p.norm_weight, self.p.norm_eps, self.p.gate_w, self.top_k,
+                renorm=self.norm_topk_prob, residual_out=residual_out, normed=nbuf,
+                gate_bias=self.p.gate_bias, scale=self.scale, has_shared_gate=self.shared_gate,
+                log2phy=l2p, rep_count=rep, num_slots=self.G * self.P, workspace=self.ws,
+                status=self.status)
+            return ro, self.forward(normed, out=out, pre=r)
         ro, normed = ops.add_rmsnorm(residual, hidden, self.p.norm_weight, self.p.norm_eps,
                                      residual_out=residual_out, normed=nbuf)
         return ro, self.forward(normed, out=out)
@@ -248,9 +261,10 @@ class MoELayer:
         return (self.overlap_shared and self.p.shared_gate_up is not None
                 and T * self.top_k <= 48 * self.P)
 
-    def _forward_local(self, x: torch.Tensor, out: Optional[torch.Tensor]) -> torch.Tensor:
+    def _forward_local(self, x: torch.Tensor, out: Optional[torch.Tensor],
+                       pre: Optional[ops.RouterOutput] = None) -> torch.Tensor:
         if not self._overlap(x.shape[0]):
-            st = self.route_and_permute(x)
+            st = self.route_and_permute(x, pre)
             self.shared_expert(x, st)
             return self.unpermute(st, self.experts_local(st), out)
         cur = torch.cuda.current_stream(self.device)
@@ -261,7 +275,7 @@ class MoELayer:
         held = DispatchState(T=x.shape[0], route=None, perm=None)
         with torch.cuda.stream(side):
             self.shared_expert(x, held)
-        st = self.route_and_permute(x)
+        st = self.route_and_permute(x, pre)
         y = self.experts_local(st)
         cur.wait_stream(side)                       # join before the combine reads it
         held.shared_out.record_stream(cur)
@@ -273,15 +287,15 @@ class MoELayer:
         # the fused forms run the bf16 tensor-core kernels; fp32 layers use the plain ones
         return self.exchange.fused and self.p.w_down.dtype == torch.bfloat16
 
-    def peer_route_dispatch(self, x: torch.Tensor) -> DispatchState:
+    def peer_route_dispatch(self, x: torch.Tensor, pre: Optional[ops.RouterOutput] = None) -> DispatchState:
         """Router, then the rows to their owners: fused permute+dispatch, or permute into
         the send buffer and a separate dispatch."""
         xg = self.exchange
         if self._fused():
-            r = self.route(x)
+            r = self.route(x, pre)
             pos_of = xg.permute_dispatch(x, r, self.p.gate_w.shape[0])
             return DispatchState(T=x.shape[0], route=r, perm=ops.PermuteOutput(None, pos_of, None, None))
-        st = self.route_and_permute(x)
+        st = self.route_and_permute(x, pre)
         xg.dispatch(st.perm.send, st.route.slot_offsets, st.T * self.top_k)
         return st
 
@@ -311,19 +325,22 @@ class MoELayer:
         back = self.exchange.wait_combine(st.T * self.top_k)
         return self.unpermute(st, back, out)
 
-    def forward_peer(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        st = self.peer_route_dispatch(x)
+    def forward_peer(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                     pre: Optional[ops.RouterOutput] = None) -> torch.Tensor:
+        st = self.peer_route_dispatch(x, pre)
         self.shared_expert(x, st)  # overlaps the other ranks' rows arriving
         self.peer_experts(st)
         return self.peer_finish(st, out)
 
-    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Routed output plus the (gated) shared-expert output for this rank's tokens."""
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                pre: Optional[ops.RouterOutput] = None) -> torch.Tensor:
+        """Routed output plus the (gated) shared-expert output for this rank's tokens
+        (pre: this batch's routing, when the caller already ran the router)."""
         if self.G > 1 and self.exchange is not None:
-            return self.forward_peer(x, out)
+            return self.forward_peer(x, out, pre)
         if self.G == 1:
-            return self._forward_local(x, out)
-        st = self.route_and_permute(x)
+            return self._forward_local(x, out, pre)
+        st = self.route_and_permute(x, pre)
         self.shared_expert(x, st)
         counts = self.exchange_counts(st)
         self.plan_exchange(st, counts)

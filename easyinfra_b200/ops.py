@@ -91,33 +91,26 @@ def router_workspace_bytes(T: int, E1: int, num_slots: int) -> int:
     return int(_lib.load().b200moe_router_workspace_bytes(T, E1, num_slots))
 
 
-def router(x: torch.Tensor, gate_w: torch.Tensor, top_k: int, *, renorm: bool,
-           gate_bias: Optional[torch.Tensor] = None, scale: float = 1.0,
-           has_shared_gate: bool = False, log2phy: Optional[torch.Tensor] = None,
-           rep_count: Optional[torch.Tensor] = None, num_slots: Optional[int] = None,
-           keep_logits: bool = False, workspace: Optional[Workspace] = None,
-           status: Optional[torch.Tensor] = None) -> RouterOutput:
-    """softmax top-k routing + replica pick + slot histogram (one call, two kernels)."""
-    _need_cuda(x, gate_w, gate_bias, log2phy, rep_count, status)
-    x = _rows_contig(x)
-    T, H = x.shape
+def _router_outputs(T, H, x_dtype, dev, gate_w, top_k, gate_bias, has_shared_gate, log2phy, rep_count,
+                    num_slots, keep_logits, workspace):
+    """Validated inputs and freshly allocated outputs of one softmax-router call."""
     E1 = gate_w.shape[0]
     E = E1 - (1 if has_shared_gate else 0)
-    if gate_w.dtype != x.dtype or gate_w.shape[1] != H:
+    if gate_w.dtype != x_dtype or gate_w.shape[1] != H:
         raise ValueError("gate_w must be [E(+1), H] with x's dtype")
     gate_w = gate_w.contiguous()
     if num_slots is None:
         num_slots = E
-    dev = x.device
-    topk_ids = torch.empty(T, top_k, dtype=torch.int32, device=dev)
-    topk_w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
-    phys = torch.empty(T, top_k, dtype=torch.int32, device=dev)
-    counts = torch.empty(num_slots, dtype=torch.int32, device=dev)
-    offsets = torch.empty(num_slots + 1, dtype=torch.int32, device=dev)
-    sg = torch.empty(T, dtype=torch.float32, device=dev) if has_shared_gate else None
-    logits = torch.empty(T, E1, dtype=torch.float32, device=dev) if keep_logits else None
-    ws_bytes = router_workspace_bytes(T, E1, num_slots)
-    ws = (workspace or Workspace(dev)).get(ws_bytes)
+    out = dict(
+        E=E, E1=E1, gate_w=gate_w, num_slots=num_slots,
+        topk_ids=torch.empty(T, top_k, dtype=torch.int32, device=dev),
+        topk_w=torch.empty(T, top_k, dtype=torch.float32, device=dev),
+        phys=torch.empty(T, top_k, dtype=torch.int32, device=dev),
+        counts=torch.empty(num_slots, dtype=torch.int32, device=dev),
+        offsets=torch.empty(num_slots + 1, dtype=torch.int32, device=dev),
+        sg=torch.empty(T, dtype=torch.float32, device=dev) if has_shared_gate else None,
+        logits=torch.empty(T, E1, dtype=torch.float32, device=dev) if keep_logits else None)
+    out["ws"] = (workspace or Workspace(dev)).get(router_workspace_bytes(T, E1, num_slots))
     if gate_bias is not None:
         # one fp32 bias per router column; the shared-expert gate column has none
         gate_bias = gate_bias.to(torch.float32).reshape(-1)
@@ -126,19 +119,83 @@ def router(x: torch.Tensor, gate_w: torch.Tensor, top_k: int, *, renorm: bool,
         if gate_bias.numel() != E1:
             raise ValueError(f"gate_bias has {gate_bias.numel()} entries, router has {E1} columns")
         gate_bias = gate_bias.contiguous()
-    max_rep = 0
+    out["gate_bias"] = gate_bias
+    out["max_rep"] = 0
     if log2phy is not None:
         log2phy = log2phy.to(torch.int32).contiguous()
         rep_count = rep_count.to(torch.int32).contiguous()
-        max_rep = log2phy.shape[1]
-    _lib.call("b200moe_router", x.data_ptr(), x.stride(0), _dtype_code(x), gate_w.data_ptr(),
-              _ptr(gate_bias), int(has_shared_gate), T, H, E, top_k, int(renorm), float(scale),
-              _ptr(log2phy), _ptr(rep_count), max_rep, num_slots, topk_ids.data_ptr(),
-              topk_w.data_ptr(), phys.data_ptr(), _ptr(sg), counts.data_ptr(),
-              offsets.data_ptr(), _ptr(logits), ws.data_ptr(), ws.numel(), _ptr(status),
-              _stream())
-    _count(2 if T else 0)
-    return RouterOutput(topk_ids, topk_w, phys, counts, offsets, sg, logits, ws)
+        out["max_rep"] = log2phy.shape[1]
+    out["log2phy"], out["rep_count"] = log2phy, rep_count
+    return out
+
+
+def _router_result(o) -> "RouterOutput":
+    return RouterOutput(o["topk_ids"], o["topk_w"], o["phys"], o["counts"], o["offsets"], o["sg"], o["logits"],
+                        o["ws"])
+
+
+def _router_tail(o, T, H, top_k, renorm, scale, has_shared_gate, status):
+    """The router arguments after x (shared by b200moe_router and b200moe_add_rmsnorm_router)."""
+    return (o["gate_w"].data_ptr(), _ptr(o["gate_bias"]), int(has_shared_gate), T, H, o["E"], top_k, int(renorm),
+            float(scale), _ptr(o["log2phy"]), _ptr(o["rep_count"]), o["max_rep"], o["num_slots"],
+            o["topk_ids"].data_ptr(), o["topk_w"].data_ptr(), o["phys"].data_ptr(), _ptr(o["sg"]),
+            o["counts"].data_ptr(), o["offsets"].data_ptr(), _ptr(o["logits"]), o["ws"].data_ptr(),
+            o["ws"].numel(), _ptr(status), _stream())
+
+
+def _router_launches(T: int) -> int:
+    # batches of up to 8 tokens run as one fused launch (logits + selection)
+    return 0 if T == 0 else (1 if T <= 8 else 2)
+
+
+def router(x: torch.Tensor, gate_w: torch.Tensor, top_k: int, *, renorm: bool,
+           gate_bias: Optional[torch.Tensor] = None, scale: float = 1.0,
+           has_shared_gate: bool = False, log2phy: Optional[torch.Tensor] = None,
+           rep_count: Optional[torch.Tensor] = None, num_slots: Optional[int] = None,
+           keep_logits: bool = False, workspace: Optional[Workspace] = None,
+           status: Optional[torch.Tensor] = None) -> RouterOutput:
+    """softmax top-k routing + replica pick + slot histogram (one call; two kernels, or
+    one for batches of up to 8 tokens)."""
+    _need_cuda(x, gate_w, gate_bias, log2phy, rep_count, status)
+    x = _rows_contig(x)
+    T, H = x.shape
+    o = _router_outputs(T, H, x.dtype, x.device, gate_w, top_k, gate_bias, has_shared_gate, log2phy, rep_count,
+                        num_slots, keep_logits, workspace)
+    _lib.call("b200moe_router", x.data_ptr(), x.stride(0), _dtype_code(x),
+              *_router_tail(o, T, H, top_k, renorm, scale, has_shared_gate, status))
+    _count(_router_launches(T))
+    return _router_result(o)
+
+
+def add_rmsnorm_router(residual: torch.Tensor, hidden: Optional[torch.Tensor], norm_weight: torch.Tensor,
+                       eps: float, gate_w: torch.Tensor, top_k: int, *, renorm: bool,
+                       residual_out: Optional[torch.Tensor] = None, normed: Optional[torch.Tensor] = None,
+                       gate_bias: Optional[torch.Tensor] = None, scale: float = 1.0,
+                       has_shared_gate: bool = False, log2phy: Optional[torch.Tensor] = None,
+                       rep_count: Optional[torch.Tensor] = None, num_slots: Optional[int] = None,
+                       workspace: Optional[Workspace] = None, status: Optional[torch.Tensor] = None):
+    """The block prologue (residual += hidden; normed = RMSNorm) and the router in one
+    call: one launch for batches of up to 8 tokens.  Returns (residual_out, normed,
+    RouterOutput); bit-identical to add_rmsnorm followed by router."""
+    _need_cuda(residual, hidden, norm_weight, gate_w, gate_bias, log2phy, rep_count, status)
+    residual = _rows_contig(residual)
+    T, H = residual.shape
+    if hidden is not None:
+        hidden = _rows_contig(hidden)
+        if hidden.stride(0) != residual.stride(0):
+            raise ValueError("residual and hidden must share a row stride")
+    ro = residual_out if residual_out is not None else torch.empty_like(residual)
+    nm = normed if normed is not None else torch.empty_like(residual)
+    if ro.stride(0) != residual.stride(0):
+        raise ValueError("residual_out must have residual's row stride")
+    o = _router_outputs(T, H, residual.dtype, residual.device, gate_w, top_k, gate_bias, has_shared_gate, log2phy,
+                        rep_count, num_slots, False, workspace)
+    _lib.call("b200moe_add_rmsnorm_router", residual.data_ptr(), _ptr(hidden),
+              norm_weight.contiguous().data_ptr(), float(eps), residual.stride(0), ro.data_ptr(), nm.data_ptr(),
+              nm.stride(0), _dtype_code(residual),
+              *_router_tail(o, T, H, top_k, renorm, scale, has_shared_gate, status))
+    _count(0 if T == 0 else (1 if T <= 8 else 3))
+    return ro, nm, _router_result(o)
 
 
 def router_sigmoid_grouped(x: torch.Tensor, gate_w: torch.Tensor, correction_bias: torch.Tensor,
@@ -176,7 +233,7 @@ def router_sigmoid_grouped(x: torch.Tensor, gate_w: torch.Tensor, correction_bia
               int(renorm), float(scale), _ptr(log2phy), _ptr(rep_count), max_rep, num_slots,
               topk_ids.data_ptr(), topk_w.data_ptr(), phys.data_ptr(), counts.data_ptr(),
               offsets.data_ptr(), _ptr(logits), ws.data_ptr(), ws.numel(), _ptr(status), _stream())
-    _count(2 if T else 0)
+    _count(_router_launches(T))
     return RouterOutput(topk_ids, topk_w, phys, counts, offsets, None, logits, ws)
 
 

@@ -104,6 +104,29 @@ B200MOE_API int b200moe_router(const void* x, int64_t ldx, int x_dtype, const vo
                    size_t workspace_bytes, int* status, void* stream);
 
 /*
+ * The block's stage-1 prologue and the router in one call: residual_out = residual +
+ * hidden, normed = weight * rmsnorm(residual_out) (as b200moe_add_rmsnorm, leading
+ * dimension ld for residual / hidden / residual_out and ld_normed for normed), then
+ * b200moe_router on normed (same remaining arguments).  For T <= 8 (decode) the whole
+ * of it is one launch: every router-column CTA builds the normed rows itself and the
+ * last CTA selects; larger batches run the two calls.  Results are bit-identical to
+ * calling b200moe_add_rmsnorm and b200moe_router.  Replaces the routing step of
+ * MoeAll2AllBlock.all2all_chunk_routing_compute (easyinfra/generation/blocks/moe/
+ * moe_all2all.py:331-343) together with Qwen3MoeSparseMoeBlock._routing
+ * (modeling_qwen3_moe.py:255-266).
+ */
+B200MOE_API int b200moe_add_rmsnorm_router(const void* residual, const void* hidden, const void* norm_weight,
+                                           float eps, int64_t ld, void* residual_out, void* normed,
+                                           int64_t ld_normed, int x_dtype, const void* gate_w,
+                                           const float* gate_bias, int has_shared_gate, int T, int H, int E, int K,
+                                           int renorm, float scale, const int32_t* log2phy,
+                                           const int32_t* rep_count, int max_rep, int num_slots,
+                                           int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                                           float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets,
+                                           float* logits_out, void* workspace, size_t workspace_bytes,
+                                           int* status, void* stream);
+
+/*
  * Router of the DeepSeek-V3 family: fp32 logits x·W_gᵀ, sigmoid scores, choice =
  * score + correction_bias, keep the topk_group groups (E / n_group consecutive
  * experts each) with the largest sum of their two best choices, top-K over the

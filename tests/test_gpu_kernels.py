@@ -327,3 +327,77 @@ def test_router_sigmoid_grouped_matches_reference(cuda_device, name):
             assert abs(mine[e] - rw) <= float(bf16_ulp(torch.tensor(rw))), (t, e)
     counts = torch.bincount(ids_o.reshape(-1), minlength=c["E"])
     assert torch.equal(out.slot_counts.cpu().long(), counts)
+
+
+@pytest.mark.parametrize("T", [1, 3, 8])
+@pytest.mark.parametrize("E,H,shared,eplb", [(128, 2048, False, True), (60, 1024, True, False), (8, 4096, False, False)])
+def test_small_batch_fused_router_equals_two_kernel_path(cuda_device, T, E, H, shared, eplb):
+    """Batches of up to 8 tokens run logits and selection as one launch; the result is
+    bit-identical to the two-kernel path: logits against the same tokens routed inside
+    a 16-token batch (one CTA per 8 tokens there too, per-token sums in the same order),
+    selection against the selection kernel run on those logits."""
+    g = torch.Generator().manual_seed(T * 131 + E)
+    E1 = E + (1 if shared else 0)
+    x16 = torch.randn(16, H, generator=g).to(torch.bfloat16).to(cuda_device)
+    w = (torch.randn(E1, H, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
+    b = (torch.randn(E1, generator=g) * 0.5).float().to(cuda_device)
+    l2p = rep = None
+    slots = E
+    if eplb:
+        phy2log = torch.cat([torch.arange(E), torch.arange(16)]).view(1, -1)
+        from easyinfra_b200.placement import Placement
+        pl = Placement(phy2log, E)
+        l2p, rep = pl.device_tables(cuda_device)
+        slots = pl.num_slots
+    kw = dict(renorm=True, gate_bias=b, scale=1.5, has_shared_gate=shared, log2phy=l2p, rep_count=rep,
+              num_slots=slots, keep_logits=True)
+    small = ops.router(x16[:T], w, 4, **kw)
+    big = ops.router(x16, w, 4, **kw)
+    sel = ops.router_from_logits(small.logits, 4, renorm=True, round_bf16=True, scale=1.5, has_shared_gate=shared,
+                                 log2phy=l2p, rep_count=rep, num_slots=slots)
+    torch.cuda.synchronize()
+    assert torch.equal(small.logits, big.logits[:T])
+    for a, c in [(small.topk_ids, sel.topk_ids), (small.topk_weights, sel.topk_weights),
+                 (small.phys_ids, sel.phys_ids), (small.slot_counts, sel.slot_counts),
+                 (small.slot_offsets, sel.slot_offsets)]:
+        assert torch.equal(a, c)
+    if shared:
+        assert torch.equal(small.shared_gate, sel.shared_gate)
+
+
+@pytest.mark.parametrize("T", [1, 5, 8, 12])
+def test_fused_prologue_router_equals_separate_calls(cuda_device, T):
+    """add_rmsnorm_router (one launch up to 8 tokens) == add_rmsnorm then router."""
+    g = torch.Generator().manual_seed(T)
+    H, E = 2048, 128
+    res = torch.randn(T, H, generator=g).to(torch.bfloat16).to(cuda_device)
+    hid = torch.randn(T, H, generator=g).to(torch.bfloat16).to(cuda_device)
+    nw = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(cuda_device)
+    w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
+    ro, nm, r = ops.add_rmsnorm_router(res, hid, nw, 1e-6, w, 8, renorm=True)
+    ro2, nm2 = ops.add_rmsnorm(res, hid, nw, 1e-6)
+    r2 = ops.router(nm2, w, 8, renorm=True)
+    torch.cuda.synchronize()
+    assert torch.equal(ro, ro2) and torch.equal(nm, nm2)
+    for a, c in [(r.topk_ids, r2.topk_ids), (r.topk_weights, r2.topk_weights), (r.phys_ids, r2.phys_ids),
+                 (r.slot_counts, r2.slot_counts), (r.slot_offsets, r2.slot_offsets)]:
+        assert torch.equal(a, c)
+
+
+@pytest.mark.parametrize("T", [2, 8])
+def test_small_batch_fused_sigmoid_router(cuda_device, T):
+    """The DeepSeek-V3 router's small-batch path (one launch) equals its selection
+    kernel on the same logits."""
+    g = torch.Generator().manual_seed(99 + T)
+    H, E = 1024, 64
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(cuda_device)
+    w = (torch.randn(E, H, generator=g) * 0.05).to(torch.bfloat16).to(cuda_device)
+    cb = (torch.randn(E, generator=g) * 0.1).float().to(cuda_device)
+    r = ops.router_sigmoid_grouped(x, w, cb, 6, n_group=8, topk_group=4, renorm=True, scale=2.5,
+                                   keep_logits=True)
+    x16 = torch.cat([x] * (16 // T + 1))[:16]   # 16 tokens: the two-kernel path
+    ref = ops.router_sigmoid_grouped(x16, w, cb, 6, n_group=8, topk_group=4, renorm=True, scale=2.5,
+                                     keep_logits=True)
+    torch.cuda.synchronize()
+    assert torch.equal(r.logits, ref.logits[:T])
+    assert torch.equal(r.topk_ids, ref.topk_ids[:T]) and torch.equal(r.topk_weights, ref.topk_weights[:T])

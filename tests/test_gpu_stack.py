@@ -14,7 +14,7 @@ from easyinfra_b200.stack import MoEStack
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("cfg,T", [("mixtral", 48), ("qwen15", 40), ("qwen3", 64)])
+@pytest.mark.parametrize("cfg,T", [("mixtral", 48), ("qwen15", 40), ("qwen3", 64), ("qwen3", 1), ("qwen15", 6)])
 def test_graph_replay_equals_eager(cuda_device, cfg, T):
     shape = C.small(C.CONFIGS[cfg], hidden=256, intermediate=128,
                     shared_intermediate=256 if C.CONFIGS[cfg].shared_intermediate else 0)
