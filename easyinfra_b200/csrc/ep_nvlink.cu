@@ -212,8 +212,10 @@ __global__ void ep_wait_comb_kernel(const __grid_constant__ EpParams p, uint32_t
   *expect = target;
 }
 
+// One warp per row in flight; up to 6 CTAs of 8 warps per SM so that large copies keep
+// enough loads outstanding to stream at HBM / NVLink speed.
 static int grid_for_rows(int64_t rows) {
-  return static_cast<int>(max64(1, min64(2 * num_sms(), (rows + 7) / 8)));
+  return static_cast<int>(max64(1, min64(6 * num_sms(), (rows + 7) / 8)));
 }
 
 int launch_ep_dispatch(const EpParams& p, const void* send, const int32_t* slot_offsets, int64_t max_rows,

@@ -19,6 +19,8 @@
 //                       replica pick, per-block slot histogram; the last CTA to
 //                       finish turns the histograms into slot counts, slot offsets
 //                       and per-(slot, block) write offsets for the permute kernel.
+#include <cstdlib>
+
 #include "kernels.cuh"
 #include "norm_row.cuh"
 
@@ -641,7 +643,14 @@ int launch_router_small_fused(const RouterLogitsParams& lp, const RouterSelectPa
 // ------------------------------------------------------------------ host launchers
 int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t stream) {
   if (p.T == 0) return 0;
-  if (p.T <= 256) {
+  // GEMV (one CTA per (8-token group, column)) up to this many tokens, tensor-core
+  // tiles above; B200MOE_ROUTER_GEMV_MAX overrides it for tuning.
+  static int gemv_max = -1;
+  if (gemv_max < 0) {
+    const char* v = getenv("B200MOE_ROUTER_GEMV_MAX");
+    gemv_max = v ? atoi(v) : 256;
+  }
+  if (p.T <= gemv_max) {
     const dim3 grid((p.T + RG - 1) / RG, p.E1);
     if (x_dtype == kDtypeBF16)
       launch_kernel(router_logits_gemv<__nv_bfloat16>, grid, dim3(256), 0, stream, p);
