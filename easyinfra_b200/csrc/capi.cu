@@ -106,6 +106,7 @@ int gemm_variant_from_env() {
 constexpr size_t kTicketBytes = 256;
 
 int tokens_per_block(int T) {
+  if (T > 32768) return 64;  // at most 1024 token blocks up to 65536 tokens
   if (T >= 16384) return 32;
   if (T >= 4096) return 16;
   return 8;
@@ -200,6 +201,7 @@ int check_select_args(int T, int E, int K, int num_slots, const int32_t* log2phy
                       const void* topk_w, const void* phys_ids, const void* slot_counts,
                       const void* slot_offsets, int has_shared_gate, const void* shared_gate) {
   if (T < 0) return fail(B200MOE_EINVAL, "T=%d < 0", T);
+  if (T > 65536) return fail(B200MOE_EUNSUPPORTED, "T=%d above 65536 tokens per call", T);
   if (E < 1 || E > 256) return fail(B200MOE_EUNSUPPORTED, "E=%d outside [1, 256]", E);
   if (K < 1 || K > 8 || K > E) return fail(B200MOE_EUNSUPPORTED, "K=%d outside [1, min(8, E)]", K);
   if (num_slots < 1 || num_slots > 8192) return fail(B200MOE_EUNSUPPORTED, "num_slots=%d", num_slots);

@@ -384,6 +384,73 @@ __device__ __forceinline__ void select_tokens(const RouterSelectParams& p, int t
   }
 }
 
+// Column pass of the last CTA over block_counts [num_slots][nb]: WRITE == false sums
+// each slot's column into hist[slot]; WRITE == true replaces the column by absolute
+// write offsets (exclusive prefix from the slot offset in hist).  SB slots per warp
+// iteration, each lane owning per_lane <= PL contiguous blocks; every load of an
+// iteration is issued before any arithmetic, so a warp has SB * PL loads in flight
+// instead of one per slot.
+template <int SB, int PL, bool WRITE>
+__device__ __forceinline__ void slot_columns(const RouterSelectParams& p, int32_t* hist, int nb) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int per_lane = (nb + 31) / 32;
+  for (int s0 = warp * SB; s0 < p.num_slots; s0 += nwarps * SB) {
+    int v[SB][PL];
+#pragma unroll
+    for (int i = 0; i < SB; ++i) {
+#pragma unroll
+      for (int k = 0; k < PL; ++k) {
+        const int b = lane * per_lane + k;
+        v[i][k] = (k < per_lane && b < nb && s0 + i < p.num_slots)
+                      ? __ldcg(p.block_counts + static_cast<int64_t>(s0 + i) * nb + b)
+                      : 0;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < SB; ++i) {
+      int part = 0;
+#pragma unroll
+      for (int k = 0; k < PL; ++k) part += v[i][k];
+      if (!WRITE) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if (lane == 0 && s0 + i < p.num_slots) hist[s0 + i] = part;
+      } else {
+        int incl = part;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int n = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += n;
+        }
+        if (s0 + i < p.num_slots) {
+          int32_t* col = p.block_counts + static_cast<int64_t>(s0 + i) * nb;
+          int run = hist[s0 + i] + incl - part;
+#pragma unroll
+          for (int k = 0; k < PL; ++k) {
+            const int b = lane * per_lane + k;
+            if (k < per_lane && b < nb) {
+              col[b] = run;
+              run += v[i][k];
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+template <bool WRITE>
+__device__ __forceinline__ void slot_columns_any(const RouterSelectParams& p, int32_t* hist, int nb) {
+  const int per_lane = (nb + 31) / 32;
+  if (per_lane <= 2)
+    slot_columns<8, 2, WRITE>(p, hist, nb);
+  else if (per_lane <= 8)
+    slot_columns<4, 8, WRITE>(p, hist, nb);
+  else
+    slot_columns<1, 32, WRITE>(p, hist, nb);  // nb <= 1024 (checked on the host)
+}
+
 // Run by every thread of the CTA that arrived last, once every CTA's histogram is in
 // block_counts: slot totals, slot offsets, absolute per-(slot, block) offsets; resets
 // the ticket.  hist is shared scratch of num_slots ints.
@@ -404,18 +471,7 @@ __device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32
       hist[s] = tot;
     }
   } else {
-    const int per_lane = (nb + 31) / 32;
-    for (int s = warp; s < p.num_slots; s += blockDim.x >> 5) {
-      const int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
-      int part = 0;
-      for (int i = 0; i < per_lane; ++i) {
-        const int b = lane * per_lane + i;
-        if (b < nb) part += __ldcg(col + b);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      if (lane == 0) hist[s] = part;
-    }
+    slot_columns_any<false>(p, hist, nb);
   }
   __syncthreads();
   if (warp == 0) {
@@ -455,30 +511,7 @@ __device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32
         }
     }
   } else {
-    const int per_lane = (nb + 31) / 32;
-    for (int s = warp; s < p.num_slots; s += blockDim.x >> 5) {
-      int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
-      int part = 0;
-      for (int i = 0; i < per_lane; ++i) {
-        const int b = lane * per_lane + i;
-        if (b < nb) part += __ldcg(col + b);
-      }
-      int incl = part;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
-      }
-      int run = hist[s] + incl - part;
-      for (int i = 0; i < per_lane; ++i) {
-        const int b = lane * per_lane + i;
-        if (b < nb) {
-          const int c = __ldcg(col + b);
-          col[b] = run;
-          run += c;
-        }
-      }
-    }
+    slot_columns_any<true>(p, hist, nb);
   }
   if (threadIdx.x == 0) *p.ticket = 0u;
 }

@@ -401,3 +401,36 @@ def test_small_batch_fused_sigmoid_router(cuda_device, T):
     torch.cuda.synchronize()
     assert torch.equal(r.logits, ref.logits[:T])
     assert torch.equal(r.topk_ids, ref.topk_ids[:T]) and torch.equal(r.topk_weights, ref.topk_weights[:T])
+
+
+@pytest.mark.parametrize("T,E,K,slots", [(136, 128, 8, 128), (256, 128, 8, 160), (1000, 64, 6, 64),
+                                         (4096, 128, 8, 128), (20000, 8, 2, 8), (40000, 16, 4, 16)])
+def test_selection_and_permute_order_at_many_token_blocks(cuda_device, T, E, K, slots):
+    """Token-block counts from 17 to 1024 (every column-scan shape of the selection's
+    last CTA): ids, slot counts and offsets, and the permute order equal the oracle's
+    stable order bit for bit."""
+    g = torch.Generator().manual_seed(T + E)
+    logits = (torch.randn(T, E, generator=g) * 2.0).to(torch.bfloat16).float()
+    l2p = rep = None
+    if slots > E:
+        from easyinfra_b200.placement import Placement
+        pl = Placement(torch.cat([torch.arange(E), torch.arange(slots - E)]).view(1, -1), E)
+        l2p, rep = pl.log2phy, pl.replica_count
+    _, ids_ref = O.route_from_logits(logits.to(torch.bfloat16), K, True, torch.bfloat16)
+    phys_ref = O.eplb_pick(ids_ref, l2p, rep) if l2p is not None else ids_ref
+    si, sk = O.permute_order(phys_ref, K)
+    r = ops.router_from_logits(logits.to(cuda_device), K, renorm=True, round_bf16=True,
+                               log2phy=None if l2p is None else l2p.to(torch.int32).to(cuda_device),
+                               rep_count=None if rep is None else rep.to(torch.int32).to(cuda_device),
+                               num_slots=slots)
+    x = torch.arange(T, dtype=torch.float32).repeat_interleave(8).view(T, 8).to(torch.bfloat16)
+    p = ops.permute(x.to(cuda_device), r, num_slots=slots, E1=E, with_indices=True)
+    torch.cuda.synchronize()
+    # probabilities order exactly as the bf16 logits do, and both sides break ties to
+    # the lowest expert id, so the selection agrees everywhere
+    assert torch.equal(r.topk_ids.cpu().long(), ids_ref.long())
+    counts = torch.bincount(r.phys_ids.cpu().long().reshape(-1), minlength=slots)
+    assert torch.equal(r.slot_counts.cpu().long(), counts)
+    assert torch.equal(r.slot_offsets.cpu().long()[1:], counts.cumsum(0))
+    assert torch.equal(p.send_token.cpu(), si)
+    assert torch.equal(p.send_slot.cpu(), sk)
