@@ -128,6 +128,10 @@ SIGNATURES = {
         c_int,
         [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
          c_void_p, c_void_p]),
+    "b200moe_ep_grouped_swiglu_recv": (
+        c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
+    "b200moe_ep_grouped_down_send_recv": (
+        c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "b200moe_ep_combine": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p,

@@ -664,7 +664,8 @@ int b200moe_gather_segments(const void* src, void* dst, int64_t row_bytes,
 // counters[0..2]: tickets of dispatch (or permute-dispatch) / collect / combine_send;
 // counters[3]: dispatch arrivals consumed; counters[4]: combine arrivals consumed;
 // counters[5]: ticket of the combine that waits itself; counters[6]: ticket of the down
-// GEMM that sends its rows.
+// GEMM that sends its rows; counters[7]: metadata arrivals consumed; counters[8]: ticket
+// of the GEMM that reads the receive region directly.
 static_assert(sizeof(cudaIpcMemHandle_t) == B200MOE_EP_HANDLE_BYTES, "IPC handle size");
 
 }  // extern "C"
@@ -790,8 +791,8 @@ int b200moe_ep_collect(const b200moe_ep_desc* ep, void* x_expert, int32_t* row_m
     return fail(B200MOE_EUNSUPPORTED, "peer row map holds at most 2^%d rows per rank", kPeerRowBits);
   p.ticket = ep->counters + 1;
   const int64_t rows = rows_hint > 0 ? rows_hint : static_cast<int64_t>(p.G) * p.cap_rows;
-  if (launch_ep_collect(p, x_expert, row_map, peer_row_map, expert_offsets, ep->counters + 3, ep->timeout_ns,
-                        rows, static_cast<cudaStream_t>(stream)))
+  if (launch_ep_collect(p, x_expert, row_map, peer_row_map, expert_offsets, ep->counters + 3, ep->counters + 7,
+                        ep->timeout_ns, rows, static_cast<cudaStream_t>(stream)))
     return fail(B200MOE_ECUDA, "ep_collect launch: %s", cudaGetErrorString(cudaGetLastError()));
   return check_launch("ep_collect");
 }
@@ -943,6 +944,84 @@ int b200moe_ep_combine(const b200moe_ep_desc* ep, const int32_t* pos_of, const f
   if (launch_combine(p, static_cast<cudaStream_t>(stream)))
     return fail(B200MOE_ECUDA, "ep_combine launch: %s", cudaGetErrorString(cudaGetLastError()));
   return check_launch("ep_combine");
+}
+
+// The two prefill GEMMs reading this rank's receive region directly (no collect).
+static int recv_gemm_launch(const b200moe_ep_desc* ep, const EpParams& e, const void* a, int64_t lda,
+                            const void* w, int P, int N, int K, int w_rows, int up_row, void* out, int64_t ldo,
+                            bool swiglu, int consume, int* status, cudaStream_t st) {
+  GemmLaunch L;
+  L.a = a;
+  L.rows_cap = static_cast<int64_t>(e.G) * e.cap_rows;
+  L.lda = lda;
+  L.w = w;
+  L.p.expert_offsets = nullptr;
+  L.p.P = P;
+  L.p.N = N;
+  L.p.K = K;
+  L.p.w_rows = w_rows;
+  L.p.up_row = up_row;
+  L.p.out = out;
+  L.p.ldo = ldo;
+  L.p.out_row_map = nullptr;
+  L.p.status = status;
+  L.p.seg_mode = 1;
+  uint8_t* mine = e.peer[e.rank];
+  L.p.seg.meta = reinterpret_cast<const int32_t*>(mine + 256);
+  L.p.seg.rows_flag = reinterpret_cast<const uint32_t*>(mine);
+  L.p.seg.meta_flag = reinterpret_cast<const uint32_t*>(mine) + 2 * e.G;
+  L.p.seg.rows_expect = ep->counters + 3;
+  L.p.seg.meta_expect = ep->counters + 7;
+  L.p.seg.ticket = ep->counters + 8;
+  L.p.seg.G = e.G;
+  L.p.seg.rank = e.rank;
+  L.p.seg.cap_rows = e.cap_rows;
+  L.p.seg.comb_rows = e.comb_rows;
+  L.p.seg.timeout_ns = ep->timeout_ns;
+  L.p.seg.consume = consume;
+  if (!swiglu) {
+    L.p.peer_out = 1;
+    for (int g = 0; g < EP_MAX_RANKS; ++g) {
+      L.p.po.base[g] = g < e.G ? e.peer[g] : nullptr;
+      L.p.po.rows[g] = g < e.G ? e.peer[g] + ep_comb_offset(e.G, e.P, e.cap_rows, e.row_bytes) : nullptr;
+    }
+    L.p.po.G = e.G;
+    L.p.po.rank = e.rank;
+    L.p.po.ticket = ep->counters + 6;
+  }
+  if (!pair_gemm_supported(L, swiglu))
+    return fail(B200MOE_EUNSUPPORTED, "receive-region GEMMs need I %% 128 == 0, H %% 256 == 0, G*P <= 512");
+  if (launch_grouped_pair(L, swiglu, st))
+    return fail(B200MOE_ECUDA, "receive-region GEMM launch: %s", cudaGetErrorString(cudaGetLastError()));
+  return check_launch(swiglu ? "ep_grouped_swiglu_recv" : "ep_grouped_down_send_recv");
+}
+
+int b200moe_ep_grouped_swiglu_recv(const b200moe_ep_desc* ep, const void* w_gate_up, int P, int H, int I, void* act,
+                                   int64_t ld_act, int* status, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams e;
+  if ((rc = ep_params(ep, &e))) return rc;
+  if (P != ep->slots_per_rank || H * 2 != ep->row_bytes || I <= 0 || !w_gate_up || !act || ld_act < I ||
+      ld_act % 8 != 0 || !aligned16(act) || !aligned16(w_gate_up))
+    return fail(B200MOE_EINVAL, "ep_grouped_swiglu_recv: P=%d H=%d I=%d (bf16 rows of the exchange)", P, H, I);
+  return recv_gemm_launch(ep, e, e.peer[e.rank] + ep_recv_offset(e.G, e.P), H, w_gate_up, P, I, H, 2 * I, I, act,
+                          ld_act, true, 1, status, static_cast<cudaStream_t>(stream));
+}
+
+int b200moe_ep_grouped_down_send_recv(const b200moe_ep_desc* ep, const void* act, int64_t ld_act, const void* w_down,
+                                      int P, int H, int I, int* status, void* stream) {
+  int rc;
+  if ((rc = device_ok())) return rc;
+  EpParams e;
+  if ((rc = ep_params(ep, &e))) return rc;
+  if (P != ep->slots_per_rank || H * 2 != ep->row_bytes || I <= 0 || !w_down || !act || ld_act < I ||
+      ld_act % 8 != 0 || !aligned16(act) || !aligned16(w_down))
+    return fail(B200MOE_EINVAL, "ep_grouped_down_send_recv: P=%d H=%d I=%d (bf16 rows of the exchange)", P, H, I);
+  if (ep->comb_rows > (int64_t(1) << kPeerRowBits))
+    return fail(B200MOE_EUNSUPPORTED, "peer rows hold at most 2^%d rows per rank", kPeerRowBits);
+  return recv_gemm_launch(ep, e, act, ld_act, w_down, P, H, I, H, 0, nullptr, H, false, 0, status,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int b200moe_ep_wait_combine(const b200moe_ep_desc* ep, void* stream) {

@@ -47,6 +47,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
     const int n = s_off[threadIdx.x + 1] - s_off[threadIdx.x];
     if (n > p.cap_rows) record_status(p.status, kStatusCapacity);
     s_n[threadIdx.x] = static_cast<int>(min64(n, p.cap_rows));
+    if (blockIdx.x == 0) ep_publish_meta(p, slot_offsets, threadIdx.x);
   }
   __syncthreads();
   const int total = s_off[G];
@@ -59,14 +60,15 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
     copy_row<false>(ep_recv_rows(p.peer[d], p) + (static_cast<int64_t>(p.rank) * p.cap_rows + j) * p.row_bytes,
                     send + static_cast<int64_t>(i) * p.row_bytes, p.row_bytes, lane);
   }
-  if (last_cta(p.ticket, &s_last) && threadIdx.x < G) ep_publish_dispatch(p, slot_offsets, threadIdx.x);
+  if (last_cta(p.ticket, &s_last) && threadIdx.x < G) ep_publish_rows(p, threadIdx.x);
 }
 
 // ------------------------------------------------------------------ collect
 // Dynamic shared memory: cnt[G*P], base[G*P], srow[G+1], eoff[P+1] (int32).
 __global__ void __launch_bounds__(256) ep_collect_kernel(const __grid_constant__ EpParams p, uint8_t* xe, int32_t* row_map,
                                                          int32_t* peer_row_map, int32_t* expert_offsets,
-                                                         uint32_t* expect, uint64_t timeout_ns) {
+                                                         uint32_t* expect, uint32_t* meta_expect,
+                                                         uint64_t timeout_ns) {
   extern __shared__ int32_t sm[];
   __shared__ int s_last;
   __shared__ uint32_t s_target;
@@ -149,6 +151,7 @@ __global__ void __launch_bounds__(256) ep_collect_kernel(const __grid_constant__
   }
   if (last_cta(p.ticket, &s_last) && threadIdx.x == 0) {
     *expect = s_target;
+    *meta_expect += 1u;  // the counts arrived with the rows; keep the meta count in step
     *p.ticket = 0u;
   }
 }
@@ -227,11 +230,11 @@ int launch_ep_dispatch(const EpParams& p, const void* send, const int32_t* slot_
 }
 
 int launch_ep_collect(const EpParams& p, void* xe, int32_t* row_map, int32_t* peer_row_map,
-                      int32_t* expert_offsets, uint32_t* expect, uint64_t timeout_ns, int64_t max_rows,
-                      cudaStream_t stream) {
+                      int32_t* expert_offsets, uint32_t* expect, uint32_t* meta_expect, uint64_t timeout_ns,
+                      int64_t max_rows, cudaStream_t stream) {
   const size_t smem = sizeof(int32_t) * (2 * p.G * p.P + p.G + 1 + p.P + 1);
   return launch_kernel(ep_collect_kernel, dim3(grid_for_rows(max_rows)), dim3(256), smem, stream, p,
-                       static_cast<uint8_t*>(xe), row_map, peer_row_map, expert_offsets, expect,
+                       static_cast<uint8_t*>(xe), row_map, peer_row_map, expert_offsets, expect, meta_expect,
                        timeout_ns) == cudaSuccess
              ? 0
              : -2;

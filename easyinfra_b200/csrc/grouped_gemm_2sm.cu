@@ -39,21 +39,27 @@ struct PairShape {
   static constexpr int N = 256;                        // accumulator columns
   static constexpr int OUT_COLS = SWIGLU ? 128 : 256;  // output columns per tile
   static constexpr int TMEM_COLS = 2 * N;              // two fp32 accumulators
-  static constexpr int CTRL_BYTES = 512 + 2 * (G2_MAXP + 1) * 4;
+  static constexpr int CTRL_BYTES = 512 + 3 * (G2_MAXP + 1) * 4 + 64;  // + segment lengths, dst rows
   static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + CTRL_BYTES;
 };
 
-// tile -> (expert, n-tile, m-tile) with 256-row m-tiles, m fastest
-__device__ __forceinline__ void pair_decode_tile(const int* prefix, const int32_t* off, int P, int tile, int& e,
-                                                 int& m, int& n) {
-  int lo = 0, hi = P - 1;
+// tile -> (group, n-tile, m-tile) with 256-row m-tiles, m fastest.  A group is an
+// expert (rows off[g] .. off[g+1]) or, reading a receive region, a (source, slot)
+// segment (rows off[g] .. off[g] + len[g]).
+__device__ __forceinline__ int group_rows(const int32_t* off, const int32_t* len, bool seg, int g) {
+  return seg ? len[g] : off[g + 1] - off[g];
+}
+
+__device__ __forceinline__ void pair_decode_tile(const int* prefix, const int32_t* off, const int32_t* len, bool seg,
+                                                 int ngroups, int tile, int& e, int& m, int& n) {
+  int lo = 0, hi = ngroups - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (prefix[mid] <= tile) lo = mid; else hi = mid - 1;
   }
   e = lo;
   const int local = tile - prefix[e];
-  const int rows = off[e + 1] - off[e];
+  const int rows = group_rows(off, len, seg, e);
   const int mt = (rows + 2 * G2_ROWS - 1) / (2 * G2_ROWS);
   n = local / mt;
   m = local - n * mt;
@@ -77,13 +83,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  int* prefix = reinterpret_cast<int*>(tmem_holder + 2);  // [P+1] tile prefix
-  int32_t* off = prefix + (G2_MAXP + 1);                   // [P+1] expert row offsets
+  int* prefix = reinterpret_cast<int*>(tmem_holder + 2);  // [groups+1] tile prefix
+  int32_t* off = prefix + (G2_MAXP + 1);                   // [groups+1] first row of each group
+  int32_t* glen = off + (G2_MAXP + 1);                     // [groups] segment rows (receive region)
+  int32_t* s_dst = glen + (G2_MAXP + 1);                   // [G] first combine row at each source
+  volatile uint32_t* s_target = reinterpret_cast<volatile uint32_t*>(s_dst + EP_MAX_RANKS);  // rows, meta
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t crank = cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int nt = (p.N + S::OUT_COLS - 1) / S::OUT_COLS;
+  const bool seg = p.seg_mode != 0;
+  const int ngroups = seg ? p.seg.G * p.P : p.P;
   pdl_trigger();
 
   if (threadIdx.x == 0) {
@@ -107,32 +118,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
   cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive / load
   pdl_wait();
   if (warp == 2) {
-    for (int base = 0; base <= p.P; base += 32) {
-      const int e = base + lane;
-      if (e <= p.P) off[e] = p.expert_offsets[e];
+    if (!seg) {
+      for (int base = 0; base <= p.P; base += 32) {
+        const int e = base + lane;
+        if (e <= p.P) off[e] = p.expert_offsets[e];
+      }
+    } else {
+      // receive-region groups: (source, slot) segments, sources from this rank onwards
+      const SegIn& sg = p.seg;
+      if (lane == 0) {
+        const uint32_t mt = *sg.meta_expect + (sg.consume ? 1u : 0u);
+        const uint32_t rt = *sg.rows_expect + (sg.consume ? 1u : 0u);
+        if (sg.consume) {
+          bool ok = true;
+          for (int s = 0; s < sg.G && ok; ++s) ok = wait_flag_geq(sg.meta_flag + s, mt, sg.timeout_ns, p.status);
+          if (!ok) record_status(p.status, kStatusTimeout);
+        }
+        s_target[0] = rt;
+        s_target[1] = mt;
+      }
+      __syncwarp();
+      if (lane < sg.G) {
+        const int src = (sg.rank + lane) % sg.G;
+        const volatile int32_t* meta = sg.meta + src * (p.P + 1);
+        int run = 0;
+        for (int q = 0; q < p.P; ++q) {
+          const int c = clamp_run(meta[q], run, sg.cap_rows);
+          off[lane * p.P + q] = static_cast<int32_t>(src * sg.cap_rows + run);
+          glen[lane * p.P + q] = c;
+          run += c;
+        }
+        int dst = meta[p.P];
+        if (dst < 0 || static_cast<int64_t>(dst) + run > sg.comb_rows) {
+          if (p.peer_out) record_status(p.status, kStatusBadIndex);
+          dst = 0;  // keeps every return row inside the source's combine region
+        }
+        s_dst[src] = dst;
+      }
     }
     __syncwarp();
     int run = 0;
-    for (int base = 0; base < p.P; base += 32) {
+    for (int base = 0; base < ngroups; base += 32) {
       const int e = base + lane;
       int c = 0;
-      if (e < p.P) c = ((off[e + 1] - off[e] + 2 * G2_ROWS - 1) / (2 * G2_ROWS)) * nt;
+      if (e < ngroups) c = ((group_rows(off, glen, seg, e) + 2 * G2_ROWS - 1) / (2 * G2_ROWS)) * nt;
       int incl = c;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += v;
       }
-      if (e < p.P) prefix[e] = run + incl - c;
+      if (e < ngroups) prefix[e] = run + incl - c;
       run += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (lane == 0) prefix[p.P] = run;
+    if (lane == 0) prefix[ngroups] = run;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const int total_tiles = prefix[p.P];
+  const int total_tiles = prefix[ngroups];
   const int num_kb = (p.K + G2_BK - 1) / G2_BK;
 
   if (warp == 0) {
@@ -142,10 +187,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      uint32_t ready = 0;  // receive region: sources whose rows have arrived
       for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
-        int e, m, n;
-        pair_decode_tile(prefix, off, p.P, tile, e, m, n);
-        const int row_a = off[e] + m * 2 * G2_ROWS + static_cast<int>(crank) * G2_ROWS;
+        int g, m, n;
+        pair_decode_tile(prefix, off, glen, seg, ngroups, tile, g, m, n);
+        const int e = seg ? g % p.P : g;  // weight slot
+        if (seg && p.seg.consume && !((ready >> (g / p.P)) & 1u)) {
+          // this tile's rows come from one source: wait (bounded) for its rows flag,
+          // then order the tensor loads after that acquire
+          const int src = (p.seg.rank + g / p.P) % p.seg.G;
+          if (!wait_flag_geq(p.seg.rows_flag + src, s_target[0], p.seg.timeout_ns, p.status))
+            record_status(p.status, kStatusTimeout);
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          ready |= 1u << (g / p.P);
+        }
+        const int row_a = off[g] + m * 2 * G2_ROWS + static_cast<int>(crank) * G2_ROWS;
         const int row_b = e * p.w_rows + n * S::OUT_COLS +
                           (SWIGLU ? (crank ? p.up_row : 0) : static_cast<int>(crank) * 128);
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -201,18 +257,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
     uint32_t acc_phase = 0;
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
     for (int tile = pair; tile < total_tiles; tile += npairs) {
-      int e, m, n;
-      pair_decode_tile(prefix, off, p.P, tile, e, m, n);
-      const int rows = off[e + 1] - off[e];
+      int g, m, n;
+      pair_decode_tile(prefix, off, glen, seg, ngroups, tile, g, m, n);
+      const int rows = group_rows(off, glen, seg, g);
       const int r = m * 2 * G2_ROWS + static_cast<int>(crank) * G2_ROWS + row_in_tile;
       const bool valid = r < rows;
-      const int64_t grow = static_cast<int64_t>(off[e]) + r;
+      const int64_t grow = static_cast<int64_t>(off[g]) + r;
       int64_t orow = grow;
       __nv_bfloat16* peer_row = nullptr;
-      if (valid && p.peer_out)
-        peer_row = static_cast<__nv_bfloat16*>(peer_out_row(p.po, p.out_row_map[grow], p.ldo * 2));
-      else if (valid && p.out_row_map != nullptr)
+      if (valid && p.peer_out) {
+        int32_t v;
+        if (seg) {
+          // row j of source src's region returns to row s_dst[src] + j of src's combine region
+          const int src = (p.seg.rank + g / p.P) % p.seg.G;
+          const int64_t j = grow - static_cast<int64_t>(src) * p.seg.cap_rows;
+          v = (src << kPeerRowBits) | static_cast<int32_t>(s_dst[src] + j);
+        } else {
+          v = p.out_row_map[grow];
+        }
+        peer_row = static_cast<__nv_bfloat16*>(peer_out_row(p.po, v, p.ldo * 2));
+      } else if (valid && p.out_row_map != nullptr) {
         orow = p.out_row_map[grow];
+      }
       int ok = 0;
       if (lane == 0) ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -296,6 +362,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
     __shared__ int s_last;
     peer_out_publish(p.po, &s_last);
   }
+  if (seg && p.seg.consume) {
+    // the last CTA records the arrivals this launch consumed
+    __shared__ int s_seg_last;
+    __syncthreads();
+    if (threadIdx.x == 0) s_seg_last = (atomicAdd(p.seg.ticket, 1u) == gridDim.x - 1);
+    __syncthreads();
+    if (s_seg_last && threadIdx.x == 0) {
+      *p.seg.rows_expect = s_target[0];
+      *p.seg.meta_expect = s_target[1];
+      *p.seg.ticket = 0u;
+    }
+  }
 }
 
 template <int STAGES, bool SWIGLU>
@@ -316,7 +394,8 @@ static int run_pair(const GemmLaunch& L, cudaStream_t stream) {
     attr_set_mask |= bit;
   }
   const int nt = (L.p.N + S::OUT_COLS - 1) / S::OUT_COLS;
-  const int64_t bound = ((L.rows_cap + 2 * G2_ROWS - 1) / (2 * G2_ROWS) + L.p.P) * static_cast<int64_t>(nt);
+  const int groups = L.p.seg_mode ? L.p.seg.G * L.p.P : L.p.P;
+  const int64_t bound = ((L.rows_cap + 2 * G2_ROWS - 1) / (2 * G2_ROWS) + groups) * static_cast<int64_t>(nt);
   const int pairs = static_cast<int>(bound < num_sms() / 2 ? bound : num_sms() / 2);
   if (pairs <= 0) return 0;
   launch_kernel(grouped_gemm_pair_kernel<STAGES, SWIGLU>, dim3(2 * pairs), dim3(G2_THREADS), S::SMEM_BYTES,
@@ -328,7 +407,7 @@ static int run_pair(const GemmLaunch& L, cudaStream_t stream) {
 // (I % 128 == 0); the down form needs H % 256 == 0.  Callers fall back to the
 // single-CTA kernel otherwise.
 bool pair_gemm_supported(const GemmLaunch& L, bool swiglu) {
-  if (L.p.P > G2_MAXP) return false;
+  if ((L.p.seg_mode ? L.p.seg.G * L.p.P : L.p.P) > G2_MAXP) return false;
   return swiglu ? (L.p.N % 128 == 0) : (L.p.N % 256 == 0);
 }
 

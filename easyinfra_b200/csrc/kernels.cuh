@@ -50,7 +50,8 @@ struct RouterSelectParams {
 constexpr int EP_MAX_RANKS = 8;
 
 // Every rank's exchange buffer (one peer-mapped allocation per rank, same layout):
-//   [0, 256)            flags: disp[G] then comb[G], u32, only ever incremented
+//   [0, 256)            flags: disp[G] (rows arrived), comb[G] (results returned),
+//                       meta[G] (counts arrived), u32, only ever incremented
 //   [256, 256 + meta)   meta: G x (P + 1) i32 — per source: rows per local slot, then
 //                       the source's first send row for this rank
 //   recv rows           G x cap_rows rows of row_bytes (region s written by source s)
@@ -146,11 +147,11 @@ __device__ __forceinline__ bool last_cta(uint32_t* ticket, int* s_last) {
   return *s_last != 0;
 }
 
-// Run by thread d (< G) of the last CTA once every row for destination d is stored and
-// fenced: d's metadata for this source (rows per slot of d clamped to cap_rows, then
-// this source's first send row for d), a system fence, then d.disp[rank] += 1.
-// Thread 0 also resets the ticket.
-__device__ __forceinline__ void ep_publish_dispatch(const EpParams& p, const int32_t* slot_offsets, int d) {
+// Thread d (< G) of the dispatching kernel's first CTA, before any row moves: d's
+// metadata for this source (rows per slot of d clamped to cap_rows, then this source's
+// first send row for d), a system fence, then d.meta[rank] += 1 — so a consumer can
+// plan its work from the counts while the rows are still in flight.
+__device__ __forceinline__ void ep_publish_meta(const EpParams& p, const int32_t* slot_offsets, int d) {
   const int P = p.P;
   int32_t* meta = ep_meta(p.peer[d], p) + p.rank * (P + 1);
   int run = 0;
@@ -160,6 +161,13 @@ __device__ __forceinline__ void ep_publish_dispatch(const EpParams& p, const int
     run += c;
   }
   meta[P] = slot_offsets[d * P];
+  __threadfence_system();
+  atomicAdd_system(ep_flags(p.peer[d]) + 2 * p.G + p.rank, 1u);
+}
+
+// Thread d (< G) of the last CTA once every row for destination d is stored and fenced:
+// d.disp[rank] += 1.  Thread 0 also resets the ticket.
+__device__ __forceinline__ void ep_publish_rows(const EpParams& p, int d) {
   __threadfence_system();
   atomicAdd_system(ep_flags(p.peer[d]) + p.rank, 1u);
   if (d == 0) *p.ticket = 0u;
@@ -222,6 +230,24 @@ struct AddNormParams {
 };
 
 // ---- grouped GEMM (grouped_gemm.cu)
+// A rows straight from this rank's exchange receive region (CTA-pair kernel, prefill
+// over NVLink): groups are (source, slot) segments instead of expert-major rows, so no
+// regroup copy runs, and a tile waits only for its own source's rows.  Sources are
+// visited starting with this rank (its rows are local).
+struct SegIn {
+  const int32_t* meta = nullptr;        // this rank's meta [G][P+1]
+  const uint32_t* rows_flag = nullptr;  // this rank's disp flags [G]
+  const uint32_t* meta_flag = nullptr;  // this rank's meta flags [G]
+  uint32_t* rows_expect = nullptr;      // arrivals consumed so far
+  uint32_t* meta_expect = nullptr;
+  uint32_t* ticket = nullptr;           // completion ticket of the consuming launch
+  int G = 0, rank = 0;
+  int64_t cap_rows = 0;
+  int64_t comb_rows = 0;  // rows of every rank's combine region (bounds the return rows)
+  uint64_t timeout_ns = 0;
+  int consume = 0;  // 1: wait for the flags and advance the counters (first GEMM of the layer)
+};
+
 // Peer output of the down GEMM (fused combine-send): out_row_map[r] = (s << 24) | row
 // sends row r to row `row` of rank s's combine region; after the last tile every CTA
 // fences at system scope and the last one adds 1 to flags[G + rank] of every rank.
@@ -260,6 +286,8 @@ struct GemmParams {
   int* status;
   int peer_out = 0;            // 1: rows go to other ranks (PeerOut), out is unused
   PeerOut po;
+  int seg_mode = 0;            // 1: A rows are an exchange receive region (SegIn)
+  SegIn seg;
 };
 
 // Grouped-GEMM kernel choice: automatic (by rows per slot), or forced for tests.
@@ -304,8 +332,8 @@ struct GemmF32Params {
 int launch_ep_dispatch(const EpParams& p, const void* send, const int32_t* slot_offsets, int64_t max_rows,
                        cudaStream_t stream);
 int launch_ep_collect(const EpParams& p, void* xe, int32_t* row_map, int32_t* peer_row_map,
-                      int32_t* expert_offsets, uint32_t* expect, uint64_t timeout_ns, int64_t max_rows,
-                      cudaStream_t stream);
+                      int32_t* expert_offsets, uint32_t* expect, uint32_t* meta_expect, uint64_t timeout_ns,
+                      int64_t max_rows, cudaStream_t stream);
 int launch_ep_combine_send(const EpParams& p, const void* y_recv, int64_t max_rows, cudaStream_t stream);
 int launch_ep_wait_comb(const EpParams& p, uint32_t* expect, uint64_t timeout_ns, cudaStream_t stream);
 

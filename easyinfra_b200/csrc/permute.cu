@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(256) permute_rows(const __grid_constant__ Perm
   pdl_trigger();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (PEER && blockIdx.x == 0 && threadIdx.x < p.ep.G) ep_publish_meta(p.ep, p.slot_offsets, threadIdx.x);
   const int t0 = blockIdx.x * p.tb;
   const int nt = min(p.tb, p.T - t0);
   const int ne = nt * p.K;
@@ -118,8 +119,7 @@ __global__ void __launch_bounds__(256) permute_rows(const __grid_constant__ Perm
     }
   }
   if (PEER) {
-    if (last_cta(p.ep.ticket, &s_last) && threadIdx.x < p.ep.G)
-      ep_publish_dispatch(p.ep, p.slot_offsets, threadIdx.x);
+    if (last_cta(p.ep.ticket, &s_last) && threadIdx.x < p.ep.G) ep_publish_rows(p.ep, threadIdx.x);
   }
 }
 

@@ -108,6 +108,7 @@ class MoELayer:
         self.exchange = exchange  # PeerExchange: the NVLink transport for G > 1
         # shared expert on a second stream at decode sizes (G == 1); B200MOE_OVERLAP_SHARED=0 off
         self.overlap_shared = os.environ.get("B200MOE_OVERLAP_SHARED", "1") != "0"
+        self.recv_gemms = os.environ.get("B200MOE_RECV_GEMMS", "1") != "0"
         self._side = None
         self.placement = placement
         self.top_k = top_k
@@ -287,6 +288,12 @@ class MoELayer:
         # the fused forms run the bf16 tensor-core kernels; fp32 layers use the plain ones
         return self.exchange.fused and self.p.w_down.dtype == torch.bfloat16
 
+    def _recv_gemms(self, hint: int) -> bool:
+        """Prefill-sized rows per slot and shapes the CTA-pair GEMMs cover: skip the
+        regroup copy.  B200MOE_RECV_GEMMS=0 keeps collect + expert-major GEMMs."""
+        return (self.recv_gemms and hint >= 256 * self.P and self.I % 128 == 0 and self.H % 256 == 0
+                and self.G * self.P <= 512)
+
     def peer_route_dispatch(self, x: torch.Tensor, pre: Optional[ops.RouterOutput] = None) -> DispatchState:
         """Router, then the rows to their owners: fused permute+dispatch, or permute into
         the send buffer and a separate dispatch."""
@@ -309,6 +316,12 @@ class MoELayer:
         # tokens of its own still receives rows from the others
         hint = max(st.T, 1) * self.top_k
         fused = self._fused()
+        if fused and self._recv_gemms(hint):
+            # prefill: the CTA-pair GEMMs read the receive region per (source, slot),
+            # starting on local rows while the others' rows still arrive
+            act = xg.grouped_swiglu_recv(self.p.w_gate_up, status=self.status)
+            xg.grouped_down_send_recv(act, self.p.w_down, status=self.status)
+            return
         xe, row_map, offs = xg.collect(rows_hint=hint, peer_rows=fused)
         act = ops.grouped_swiglu(xe, offs, self.p.w_gate_up, out=xg.act, status=self.status, rows_hint=hint)
         if fused:

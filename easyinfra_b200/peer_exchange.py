@@ -80,7 +80,7 @@ class PeerExchange:
         self.recv = raw[self.recv_off:self.recv_off + rows * self.row_bytes].view(dtype).view(rows, hidden)
         self.comb = raw[self.comb_off:self.comb_off + self.comb_rows * self.row_bytes].view(dtype).view(
             self.comb_rows, hidden)
-        self.counters = torch.zeros(8, dtype=torch.int32, device=device)
+        self.counters = torch.zeros(16, dtype=torch.int32, device=device)
         self.status = status
         self.x_expert = torch.empty(rows, hidden, dtype=dtype, device=device)
         self.act = torch.empty(rows, inter, dtype=dtype, device=device)
@@ -264,3 +264,26 @@ class PeerExchange:
                   o.data_ptr() if T else None, o.stride(0) if T else self.H, ops._stream())
         ops._count(1)
         return o
+
+    # ------------------------------------------------------------ prefill, no regroup
+    def grouped_swiglu_recv(self, w_gate_up: torch.Tensor, status: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """SwiGLU GEMM reading the receive region per (source, slot) segment; rows of
+        each source are used as soon as they arrive.  Returns act (receive-region order)."""
+        P, twoI, H = w_gate_up.shape
+        I = twoI // 2
+        ops._hook("grouped_swiglu", "start")
+        _lib.call("b200moe_ep_grouped_swiglu_recv", self._p(), w_gate_up.data_ptr(), P, H, I, self.act.data_ptr(),
+                  self.act.stride(0), ops._ptr(status), ops._stream())
+        ops._hook("grouped_swiglu", "end")
+        ops._count(1)
+        return self.act
+
+    def grouped_down_send_recv(self, act: torch.Tensor, w_down: torch.Tensor,
+                               status: Optional[torch.Tensor] = None) -> None:
+        """Down GEMM on receive-region-ordered act; rows go straight back to their senders."""
+        P, H, I = w_down.shape
+        ops._hook("grouped_down", "start")
+        _lib.call("b200moe_ep_grouped_down_send_recv", self._p(), act.data_ptr(), act.stride(0), w_down.data_ptr(),
+                  P, H, I, ops._ptr(status), ops._stream())
+        ops._hook("grouped_down", "end")
+        ops._count(1)

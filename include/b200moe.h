@@ -315,7 +315,7 @@ B200MOE_API int b200moe_grouped_down_ex(const void* act, int64_t ld_act, int64_t
  *                            the expert outputs in send order for b200moe_combine.
  * Each rank creates one buffer with b200moe_ep_alloc, exchanges the 64-byte handles
  * (any host collective), maps every peer's with b200moe_ep_open and fills a
- * b200moe_ep_desc.  counters (8 x uint32, device, zeroed once) hold the kernels'
+ * b200moe_ep_desc.  counters (16 x uint32, device, zeroed once) hold the kernels'
  * tickets and how many arrivals this rank consumed; every rank must issue the four
  * calls in the same order.  Every wait is bounded by timeout_ns; on timeout the
  * status word gets B200MOE_STATUS_TIMEOUT and the kernel proceeds with what arrived
@@ -334,7 +334,7 @@ typedef struct b200moe_ep_desc {
   int row_bytes;                    /* H * element bytes, multiple of 16 */
   int64_t cap_rows;                 /* rows one source may send to one rank */
   int64_t comb_rows;                /* rows this rank sends per layer at most (T * K) */
-  uint32_t* counters;               /* device, 8 x uint32, zero before the first call */
+  uint32_t* counters;               /* device, 16 x uint32, zero before the first call */
   int* status;                      /* device status word (nullable) */
   uint64_t timeout_ns;
 } b200moe_ep_desc;
@@ -389,6 +389,24 @@ B200MOE_API int b200moe_ep_grouped_down_send(const b200moe_ep_desc* ep, const vo
                                              int64_t rows_cap, int64_t rows_hint, const int32_t* expert_offsets,
                                              int P, int H, int I, const void* w_down,
                                              const int32_t* peer_row_map, int* status, void* stream);
+/*
+ * Prefill without the regroup copy: the CTA-pair grouped GEMMs read this rank's
+ * receive region directly, one tile group per (source rank, local slot) segment,
+ * sources visited from this rank onwards.  b200moe_ep_grouped_swiglu_recv waits
+ * (bounded) for every source's counts, plans its tiles from them, and lets each tile
+ * wait only for its own source's rows — so the GEMM starts on local rows while the
+ * other ranks' rows are still crossing NVLink; act gets the SwiGLU rows in
+ * receive-region order (world_size * cap_rows rows).  b200moe_ep_grouped_down_send_recv
+ * then returns every down-projection row straight into the combine region of the rank
+ * that sent it (as b200moe_ep_grouped_down_send).  Use in place of b200moe_ep_collect
+ * + the two GEMMs, after b200moe_ep_permute_dispatch; needs I % 128 == 0,
+ * H % 256 == 0 and world_size * slots_per_rank <= 512.
+ */
+B200MOE_API int b200moe_ep_grouped_swiglu_recv(const b200moe_ep_desc* ep, const void* w_gate_up, int P, int H,
+                                               int I, void* act, int64_t ld_act, int* status, void* stream);
+B200MOE_API int b200moe_ep_grouped_down_send_recv(const b200moe_ep_desc* ep, const void* act, int64_t ld_act,
+                                                  const void* w_down, int P, int H, int I, int* status,
+                                                  void* stream);
 B200MOE_API int b200moe_ep_combine(const b200moe_ep_desc* ep, const int32_t* pos_of, const float* topk_w, int T,
                                    int K, int H, int dtype, const void* shared, int64_t lds,
                                    const float* shared_gate, void* out, int64_t ldo, void* stream);

@@ -89,8 +89,8 @@ def test_peer_exchange_matches_host_planned_path(cuda_device, name, fused):
                 assert torch.equal(outs[r], ref[r]), (name, it, r)
         for xg in xgs:
             c = xg.counters.cpu().tolist()
-            assert c[:3] == [0, 0, 0] and c[5:] == [0, 0, 0], f"tickets must return to zero: {c}"
-            assert c[3] == 3 and c[4] == 3, c
+            assert [c[i] for i in (0, 1, 2, 5, 6, 8)] == [0] * 6, f"tickets must return to zero: {c}"
+            assert c[3] == 3 and c[4] == 3 and c[7] == 3, c   # rows, results, counts consumed
     finally:
         for xg in xgs:
             xg.close()
@@ -202,6 +202,35 @@ def test_peer_exchange_with_prefill_gemm_kernels(cuda_device, name, variant, mon
             assert int(status.item()) == 0
             for r in range(case["G"]):
                 assert torch.equal(outs[r], ref[r]), (name, variant, r)
+    finally:
+        for xg in xgs:
+            xg.close()
+
+
+@pytest.mark.parametrize("name,T", [("mixtral_g2", 640), ("dsv2_g2", 1400)])
+def test_peer_exchange_receive_region_gemms(cuda_device, name, T):
+    """Prefill-sized batches: the CTA-pair GEMMs read the receive region per (source,
+    slot) segment (no regroup copy) and wait per source; the layer equals the NCCL
+    transport's data path bit for bit, call after call, and the arrival counters stay
+    in step."""
+    case = cases.CASES[name]
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    shape, layers = _layers(case, cuda_device, status)
+    assert layers[0]._recv_gemms(T * shape.top_k)
+    xs = [C.hidden_states(shape, T, rank=r).to(cuda_device) for r in range(case["G"])]
+    ref = _nccl_path(layers, xs)
+    xgs = _attach(layers, shape, T, cuda_device, status, True)
+    try:
+        for it in range(2):
+            outs = forward_peer_single_device(layers, xs)
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0, it
+            for r in range(case["G"]):
+                assert torch.equal(outs[r], ref[r]), (name, it, r)
+        for xg in xgs:
+            c = xg.counters.cpu().tolist()
+            assert [c[i] for i in (0, 1, 2, 5, 6, 8)] == [0] * 6, c
+            assert c[3] == 2 and c[4] == 2 and c[7] == 2, c
     finally:
         for xg in xgs:
             xg.close()
