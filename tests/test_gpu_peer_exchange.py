@@ -234,3 +234,40 @@ def test_peer_exchange_receive_region_gemms(cuda_device, name, T):
     finally:
         for xg in xgs:
             xg.close()
+
+
+@pytest.mark.parametrize("cfg,G,T", [("mixtral", 8, 160), ("qwen3", 8, 700)])
+def test_eight_rank_receive_region_gemms(cuda_device, cfg, G, T):
+    """Eight emulated ranks at prefill size through the receive-region GEMMs (Mixtral:
+    one expert per rank; Qwen3: the 160-slot EasyBalance map, 20 slots per rank)
+    equal the NCCL transport's data path bit for bit."""
+    base = C.CONFIGS[cfg]
+    shape = C.small(base, hidden=512, intermediate=256, shared_intermediate=0)
+    if cfg == "qwen3":
+        pl = Placement(C.load_placement(shape.placement, 0, G), shape.num_experts)
+    else:
+        pl = Placement.default(shape.num_experts, G)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    gw = C.router_weight(shape, 0)
+    gb = C.gate_bias(shape, 0)
+    P = pl.slots_per_rank
+    wgu_all, wd_all = C.expert_weights(shape, 0, pl.phy2log.reshape(-1).tolist())
+    layers = []
+    for r in range(G):
+        params = LayerParams(gw.to(cuda_device), wgu_all[r * P:(r + 1) * P].to(cuda_device),
+                             wd_all[r * P:(r + 1) * P].to(cuda_device),
+                             None if gb is None else gb.to(shape.dtype).float().to(cuda_device))
+        layers.append(MoELayer(params, pl, shape.top_k, shape.norm_topk_prob, rank=r, status=status))
+    assert layers[0]._recv_gemms(T * shape.top_k)
+    xs = [C.hidden_states(shape, T, rank=r).to(cuda_device) for r in range(G)]
+    ref = _nccl_path(layers, xs)
+    xgs = _attach(layers, shape, T, cuda_device, status, True)
+    try:
+        outs = forward_peer_single_device(layers, xs)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        for r in range(G):
+            assert torch.equal(outs[r], ref[r]), (cfg, r)
+    finally:
+        for xg in xgs:
+            xg.close()
