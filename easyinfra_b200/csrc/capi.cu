@@ -3,6 +3,7 @@
 // This layer validates arguments, lays out the router workspace, picks kernel
 // configurations and launches on the caller's stream.  It never throws across the
 // ABI and allocates device memory only in b200moe_ep_alloc (the exchange buffer).
+#include <atomic>
 #include <cstdarg>
 #include <cstdlib>
 #include <cstdio>
@@ -15,24 +16,24 @@
 namespace b200moe {
 
 bool pdl_enabled() {
-  static int cached = -1;
-  if (cached < 0) {
+  static const bool enabled = [] {
     const char* v = getenv("B200MOE_PDL");
-    cached = (v != nullptr && v[0] == '0') ? 0 : 1;
-  }
-  return cached == 1;
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return enabled;
 }
 
 int num_sms() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];  // zero-initialised (static storage)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    cached[dev].store(n, std::memory_order_relaxed);
   }
-  return cached[dev];
+  return n;
 }
 
 // ------------------------------------------------------------------ segment gather

@@ -23,6 +23,8 @@
 //   * no cluster launch: every CTA loads its own tiles with plain TMA loads.
 // Every mbarrier wait is bounded; on timeout the CTA records kStatusTimeout, drains
 // and frees its TMEM.
+#include <atomic>
+
 #include "kernels.cuh"
 
 namespace b200moe {
@@ -311,14 +313,14 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
+  static const EncodeTiledFn fn = [] {  // looked up once, thread-safe initialisation
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
+      return reinterpret_cast<EncodeTiledFn>(ptr);
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
   return fn;
 }
 
@@ -350,15 +352,15 @@ static int run_gemm(const GemmLaunch& L, cudaStream_t stream) {
   // Request at least half the SM's shared memory so two CTAs never share one SM
   // (each holds TMEM_COLS of the 512 TMEM columns for its whole lifetime).
   const int smem = S::SMEM_BYTES > 120 * 1024 ? S::SMEM_BYTES : 120 * 1024;
-  static uint64_t attr_set_mask = 0;  // one bit per device ordinal
+  static std::atomic<uint64_t> attr_set_mask{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_set_mask & bit)) {
+  if (!(attr_set_mask.load(std::memory_order_acquire) & bit)) {
     if (cudaFuncSetAttribute(grouped_gemm_kernel<BN, STAGES, SWIGLU, BMA>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return -3;
-    attr_set_mask |= bit;
+    attr_set_mask.fetch_or(bit, std::memory_order_release);
   }
   const int nt = (L.p.N + S::OUT_COLS - 1) / S::OUT_COLS;
   const int64_t bound = ((L.rows_cap + BMA - 1) / BMA + L.p.P) * static_cast<int64_t>(nt);

@@ -21,6 +21,8 @@
 // Every mbarrier wait is bounded (kWaitLimitNs); both CTAs meet at a cluster barrier
 // after initialisation and before TMEM is freed.  No load is shared across CTAs:
 // each CTA's TMA writes only its own shared memory.
+#include <atomic>
+
 #include "kernels.cuh"
 
 namespace b200moe {
@@ -383,15 +385,15 @@ static int run_pair(const GemmLaunch& L, cudaStream_t stream) {
   CUtensorMap ma, mb;
   if (make_tma_map_2d(&ma, L.a, L.rows_cap, L.p.K, L.lda, G2_ROWS) != 0) return -1;
   if (make_tma_map_2d(&mb, L.w, static_cast<int64_t>(L.p.P) * L.p.w_rows, L.p.K, L.p.K, 128) != 0) return -1;
-  static uint64_t attr_set_mask = 0;  // one bit per device ordinal
+  static std::atomic<uint64_t> attr_set_mask{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_set_mask & bit)) {
+  if (!(attr_set_mask.load(std::memory_order_acquire) & bit)) {
     if (cudaFuncSetAttribute(grouped_gemm_pair_kernel<STAGES, SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              S::SMEM_BYTES) != cudaSuccess)
       return -3;
-    attr_set_mask |= bit;
+    attr_set_mask.fetch_or(bit, std::memory_order_release);
   }
   const int nt = (L.p.N + S::OUT_COLS - 1) / S::OUT_COLS;
   const int groups = L.p.seg_mode ? L.p.seg.G * L.p.P : L.p.P;

@@ -13,6 +13,8 @@
 //     store is one coalesced 64-byte run; for SwiGLU the up half (lanes 64..127) is
 //     handed to the gate warps through shared memory;
 //   * per-CTA TMA loads only (no clusters), bounded mbarrier waits.
+#include <atomic>
+
 #include "kernels.cuh"
 
 namespace b200moe {
@@ -275,15 +277,15 @@ static int run_wm(const GemmLaunch& L, cudaStream_t stream) {
     return -1;
   if (make_tma_map_2d(&mx, L.a, L.rows_cap, L.p.K, L.lda, NTOK) != 0) return -1;
   const int smem = S::SMEM_BYTES > 120 * 1024 ? S::SMEM_BYTES : 120 * 1024;
-  static uint64_t attr_set_mask = 0;
+  static std::atomic<uint64_t> attr_set_mask{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_set_mask & bit)) {
+  if (!(attr_set_mask.load(std::memory_order_acquire) & bit)) {
     if (cudaFuncSetAttribute(grouped_gemm_wm_kernel<NTOK, STAGES, SWIGLU>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return -3;
-    attr_set_mask |= bit;
+    attr_set_mask.fetch_or(bit, std::memory_order_release);
   }
   const int nt = (L.p.N + S::FEAT - 1) / S::FEAT;
   const int64_t bound = ((L.rows_cap + NTOK - 1) / NTOK + L.p.P) * static_cast<int64_t>(nt);

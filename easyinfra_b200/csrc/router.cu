@@ -21,6 +21,8 @@
 //                       and per-(slot, block) write offsets for the permute kernel.
 #include <cstdlib>
 
+#include <atomic>
+
 #include "kernels.cuh"
 #include "norm_row.cuh"
 
@@ -649,17 +651,17 @@ bool router_small_fused_ok(int T, int H, int x_dtype, int num_slots, int scoring
 
 int launch_router_small_fused(const RouterLogitsParams& lp, const RouterSelectParams& sp, const AddNormParams* np,
                               int x_dtype, cudaStream_t stream) {
-  static uint64_t attr_set_mask = 0;  // one bit per device ordinal
+  static std::atomic<uint64_t> attr_set_mask{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
-  if (!(attr_set_mask & bit)) {
+  if (!(attr_set_mask.load(std::memory_order_acquire) & bit)) {
     if (cudaFuncSetAttribute(router_small_fused<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kFusedSmemMax)) != cudaSuccess ||
         cudaFuncSetAttribute(router_small_fused<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kFusedSmemMax)) != cudaSuccess)
       return -3;
-    attr_set_mask |= bit;
+    attr_set_mask.fetch_or(bit, std::memory_order_release);
   }
   AddNormParams none{};
   const size_t smem = router_small_fused_smem(lp.T, lp.H, x_dtype, sp.num_slots, sp.scoring);
@@ -678,11 +680,10 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
   if (p.T == 0) return 0;
   // GEMV (one CTA per (8-token group, column)) up to this many tokens, tensor-core
   // tiles above; B200MOE_ROUTER_GEMV_MAX overrides it for tuning.
-  static int gemv_max = -1;
-  if (gemv_max < 0) {
+  static const int gemv_max = [] {
     const char* v = getenv("B200MOE_ROUTER_GEMV_MAX");
-    gemv_max = v ? atoi(v) : 256;
-  }
+    return v ? atoi(v) : 256;
+  }();
   if (p.T <= gemv_max) {
     const dim3 grid((p.T + RG - 1) / RG, p.E1);
     if (x_dtype == kDtypeBF16)
@@ -698,11 +699,11 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
     while (cols > 8 && tok_blocks * ((p.E1 + cols - 1) / cols) < 2 * num_sms()) cols -= 8;
     dim3 grid(tok_blocks, (p.E1 + cols - 1) / cols);
     const size_t stage_bytes = static_cast<size_t>(RL_TOK + cols) * RL_LD * sizeof(__nv_bfloat16);
-    static uint64_t attr_set_mask = 0;  // one bit per device ordinal
+    static std::atomic<uint64_t> attr_set_mask{0};  // one bit per device ordinal
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
-    if (!(attr_set_mask & bit)) {
+    if (!(attr_set_mask.load(std::memory_order_acquire) & bit)) {
       const int max4 = 4 * (RL_TOK + RL_MAXNT * 8) * RL_LD * sizeof(__nv_bfloat16);
       const int max8 = 8 * (RL_TOK + 24) * RL_LD * sizeof(__nv_bfloat16);
       if (cudaFuncSetAttribute(router_logits_bf16<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max4) !=
@@ -710,7 +711,7 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
           cudaFuncSetAttribute(router_logits_bf16<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max8) !=
               cudaSuccess)
         return -3;
-      attr_set_mask |= bit;
+      attr_set_mask.fetch_or(bit, std::memory_order_release);
     }
     if (cols <= 24)
       launch_kernel(router_logits_bf16<8>, grid, dim3(128), 8 * stage_bytes, stream, p, cols);

@@ -58,3 +58,22 @@ def test_no_cluster_shared_loads_in_sources():
             if needle in line:
                 assert "tcgen05.commit" in line, f"{f}:{i}"
                 assert "cp.async" not in line and "bulk" not in line, f"{f}:{i}"
+
+
+def test_exchange_descriptor_and_layout_without_a_gpu():
+    """The ctypes mirror of b200moe_ep_desc has the C layout, and the exchange buffer
+    layout (flags, per-source counts, receive rows, combine rows) is what the header
+    describes."""
+    assert ctypes.sizeof(_lib.EpDesc) == 8 * 8 + 4 * 4 + 2 * 8 + 2 * 8 + 8
+    from easyinfra_b200.peer_exchange import layout
+    G, P, cap, comb, row = 2, 4, 128, 128, 1024
+    recv, comb_off, total = layout(G, P, cap, comb, row)
+    assert recv == 256 + 256                      # flags, then G*(P+1) ints rounded to 256 B
+    assert comb_off == recv + G * cap * row
+    assert total == comb_off + comb * row
+    recv8, _, _ = layout(8, 64, 16, 16, 4096)
+    assert recv8 == 256 + ((8 * 65 * 4 + 255) // 256) * 256
+    lib = _lib.load()
+    bad = ctypes.c_int64()
+    assert lib.b200moe_ep_layout(9, 4, 1, 1, 1024, None, None, ctypes.byref(bad)) != 0   # > 8 ranks
+    assert lib.b200moe_ep_layout(2, 4, 1, 1, 1000, None, None, ctypes.byref(bad)) != 0   # rows not 16-B multiples
