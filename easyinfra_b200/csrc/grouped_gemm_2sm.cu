@@ -22,6 +22,7 @@
 // after initialisation and before TMEM is freed.  No load is shared across CTAs:
 // each CTA's TMA writes only its own shared memory.
 #include <atomic>
+#include <cstdlib>
 
 #include "kernels.cuh"
 
@@ -52,8 +53,11 @@ __device__ __forceinline__ int group_rows(const int32_t* off, const int32_t* len
   return seg ? len[g] : off[g + 1] - off[g];
 }
 
+// ng > 0: n-tiles are visited in bands of ng, and inside a band the tiles of one
+// m-tile are consecutive — a wave of concurrent tiles then covers a compact block of
+// m x n tiles, so both operands are reused from L2 (ng = 0: m fastest).
 __device__ __forceinline__ void pair_decode_tile(const int* prefix, const int32_t* off, const int32_t* len, bool seg,
-                                                 int ngroups, int tile, int& e, int& m, int& n) {
+                                                 int ngroups, int tile, int nt, int ng, int& e, int& m, int& n) {
   int lo = 0, hi = ngroups - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -63,8 +67,16 @@ __device__ __forceinline__ void pair_decode_tile(const int* prefix, const int32_
   const int local = tile - prefix[e];
   const int rows = group_rows(off, len, seg, e);
   const int mt = (rows + 2 * G2_ROWS - 1) / (2 * G2_ROWS);
-  n = local / mt;
-  m = local - n * mt;
+  if (ng <= 0) {
+    n = local / mt;
+    m = local - n * mt;
+    return;
+  }
+  const int band = local / (mt * ng);
+  const int nb = min(ng, nt - band * ng);  // n-tiles in this band
+  const int li = local - band * mt * ng;
+  m = li / nb;
+  n = band * ng + (li - m * nb);
 }
 
 __device__ __forceinline__ float pair_silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
@@ -192,7 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
       uint32_t ready = 0;  // receive region: sources whose rows have arrived
       for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
         int g, m, n;
-        pair_decode_tile(prefix, off, glen, seg, ngroups, tile, g, m, n);
+        pair_decode_tile(prefix, off, glen, seg, ngroups, tile, nt, p.tile_band, g, m, n);
         const int e = seg ? g % p.P : g;  // weight slot
         if (seg && p.seg.consume && !((ready >> (g / p.P)) & 1u)) {
           // this tile's rows come from one source: wait (bounded) for its rows flag,
@@ -260,7 +272,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
     for (int tile = pair; tile < total_tiles; tile += npairs) {
       int g, m, n;
-      pair_decode_tile(prefix, off, glen, seg, ngroups, tile, g, m, n);
+      pair_decode_tile(prefix, off, glen, seg, ngroups, tile, nt, p.tile_band, g, m, n);
       const int rows = group_rows(off, glen, seg, g);
       const int r = m * 2 * G2_ROWS + static_cast<int>(crank) * G2_ROWS + row_in_tile;
       const bool valid = r < rows;
@@ -379,8 +391,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
 }
 
 template <int STAGES, bool SWIGLU>
-static int run_pair(const GemmLaunch& L, cudaStream_t stream) {
+static int run_pair(const GemmLaunch& L0, cudaStream_t stream) {
   using S = PairShape<STAGES, SWIGLU>;
+  // B200MOE_PAIR_BAND=k visits n-tiles in bands of k (0 / unset: m fastest)
+  static const int band = [] {
+    const char* v = getenv("B200MOE_PAIR_BAND");
+    return v ? atoi(v) : 0;
+  }();
+  GemmLaunch L = L0;
+  L.p.tile_band = band;
   static_assert(S::SMEM_BYTES <= 232448, "shared memory");
   CUtensorMap ma, mb;
   if (make_tma_map_2d(&ma, L.a, L.rows_cap, L.p.K, L.lda, G2_ROWS) != 0) return -1;

@@ -288,6 +288,7 @@ struct GemmParams {
   PeerOut po;
   int seg_mode = 0;            // 1: A rows are an exchange receive region (SegIn)
   SegIn seg;
+  int tile_band = 0;           // CTA-pair kernel: n-tile band of the tile order (0: m fastest)
 };
 
 // Grouped-GEMM kernel choice: automatic (by rows per slot), or forced for tests.
