@@ -40,7 +40,9 @@ constexpr int RL_MAXNT = 17;     // up to 136 logit columns per pass
 
 // RL_STAGES chunks in flight: 8 for narrow column groups (few router columns: the
 // kernel is a pure stream over x and needs the most bytes in flight), 4 otherwise.
-template <int RL_STAGES>
+// NT: compile-time bound on the CTA's 8-column tiles, so a router with few experts
+// issues only the MMAs it needs.
+template <int RL_STAGES, int NT>
 __global__ void __launch_bounds__(128) router_logits_bf16(const __grid_constant__ RouterLogitsParams p,
                                                           int cols_per_cta) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -76,9 +78,9 @@ __global__ void __launch_bounds__(128) router_logits_bf16(const __grid_constant_
     }
   };
 
-  float acc[RL_MAXNT][4];
+  float acc[NT][4];
 #pragma unroll
-  for (int i = 0; i < RL_MAXNT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
 #pragma unroll
   for (int c = 0; c < RL_STAGES - 1; ++c) {
@@ -99,7 +101,7 @@ __global__ void __launch_bounds__(128) router_logits_bf16(const __grid_constant_
       const uint32_t a2 = *reinterpret_cast<const uint32_t*>(xs + ar * RL_LD + k0 + ac + 8);
       const uint32_t a3 = *reinterpret_cast<const uint32_t*>(xs + (ar + 8) * RL_LD + k0 + ac + 8);
 #pragma unroll
-      for (int j = 0; j < RL_MAXNT; ++j) {
+      for (int j = 0; j < NT; ++j) {
         if (j < nt) {
           const int bn = j * 8 + (lane >> 2);
           const uint32_t b0 = *reinterpret_cast<const uint32_t*>(ws + bn * RL_LD + k0 + ac);
@@ -120,7 +122,7 @@ __global__ void __launch_bounds__(128) router_logits_bf16(const __grid_constant_
   // C fragment: c0,c1 -> (row lane/4, cols 2*(lane%4)+{0,1}); c2,c3 -> row + 8.
   const int r0 = tok0 + warp * 16 + (lane >> 2);
 #pragma unroll
-  for (int j = 0; j < RL_MAXNT; ++j) {
+  for (int j = 0; j < NT; ++j) {
     if (j < nt) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -695,8 +697,10 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
   if (x_dtype == kDtypeBF16) {
     const int tok_blocks = (p.T + RL_TOK - 1) / RL_TOK;
     // Enough CTAs to cover the SMs: narrow column groups when the token count is small.
-    int cols = RL_MAXNT * 8;
-    while (cols > 8 && tok_blocks * ((p.E1 + cols - 1) / cols) < 2 * num_sms()) cols -= 8;
+    // one column group when there are enough token blocks to cover the SMs (x is read
+    // once); narrower groups only for short batches
+    int cols = min(RL_MAXNT * 8, ((p.E1 + 7) / 8) * 8);
+    while (cols > 8 && tok_blocks * ((p.E1 + cols - 1) / cols) < num_sms()) cols -= 8;
     dim3 grid(tok_blocks, (p.E1 + cols - 1) / cols);
     const size_t stage_bytes = static_cast<size_t>(RL_TOK + cols) * RL_LD * sizeof(__nv_bfloat16);
     static std::atomic<uint64_t> attr_set_mask{0};  // one bit per device ordinal
@@ -704,19 +708,25 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (!(attr_set_mask.load(std::memory_order_acquire) & bit)) {
-      const int max4 = 4 * (RL_TOK + RL_MAXNT * 8) * RL_LD * sizeof(__nv_bfloat16);
-      const int max8 = 8 * (RL_TOK + 24) * RL_LD * sizeof(__nv_bfloat16);
-      if (cudaFuncSetAttribute(router_logits_bf16<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max4) !=
-              cudaSuccess ||
-          cudaFuncSetAttribute(router_logits_bf16<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max8) !=
-              cudaSuccess)
+      auto set = [](const void* k, int bytes) {
+        return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+      };
+      const int b = RL_LD * sizeof(__nv_bfloat16);
+      if (!set(reinterpret_cast<const void*>(router_logits_bf16<8, 1>), 8 * (RL_TOK + 8) * b) ||
+          !set(reinterpret_cast<const void*>(router_logits_bf16<8, 3>), 8 * (RL_TOK + 24) * b) ||
+          !set(reinterpret_cast<const void*>(router_logits_bf16<4, 8>), 4 * (RL_TOK + 64) * b) ||
+          !set(reinterpret_cast<const void*>(router_logits_bf16<4, RL_MAXNT>), 4 * (RL_TOK + RL_MAXNT * 8) * b))
         return -3;
       attr_set_mask.fetch_or(bit, std::memory_order_release);
     }
-    if (cols <= 24)
-      launch_kernel(router_logits_bf16<8>, grid, dim3(128), 8 * stage_bytes, stream, p, cols);
+    if (cols <= 8)
+      launch_kernel(router_logits_bf16<8, 1>, grid, dim3(128), 8 * stage_bytes, stream, p, cols);
+    else if (cols <= 24)
+      launch_kernel(router_logits_bf16<8, 3>, grid, dim3(128), 8 * stage_bytes, stream, p, cols);
+    else if (cols <= 64)
+      launch_kernel(router_logits_bf16<4, 8>, grid, dim3(128), 4 * stage_bytes, stream, p, cols);
     else
-      launch_kernel(router_logits_bf16<4>, grid, dim3(128), 4 * stage_bytes, stream, p, cols);
+      launch_kernel(router_logits_bf16<4, RL_MAXNT>, grid, dim3(128), 4 * stage_bytes, stream, p, cols);
   } else {
     const int grid = (p.T * 32 + 255) / 256;
     launch_kernel(router_logits_f32, dim3(grid), dim3(256), 0, stream, p);

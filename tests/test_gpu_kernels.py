@@ -273,7 +273,9 @@ def test_add_rmsnorm_matches_reference_prologue(cuda_device, dtype, H):
 
 
 @pytest.mark.parametrize("T,E1,H,bias", [(600, 8, 4096, False), (1000, 65, 2048, True), (300, 137, 512, True),
-                                         (7, 128, 2048, True), (256, 61, 2048, False)])
+                                         (7, 128, 2048, True), (256, 61, 2048, False),
+                                         # >= one token block per SM: every column-tile width of the tiles
+                                         (10000, 20, 1024, True), (10000, 64, 1024, False), (10000, 130, 512, True)])
 def test_router_logits_paths_match_cpu_linear(cuda_device, T, E1, H, bias):
     """Both logit kernels (tensor-core tiles for T > 256, one warp per (column, 8 tokens)
     for T <= 256) against F.linear in bf16 on the CPU: equal up to 1-ulp bf16 rounding
