@@ -20,6 +20,10 @@
 // (moe_all2all.py:291-307) as a gather: one warp per token reads its K expert rows,
 // accumulates w_k * y_k in fp32 and writes the token row once (no atomics).  The
 // optional shared-expert term adds gate[t] * shared[t] (gate == 1 when absent).
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+
 #include "kernels.cuh"
 
 namespace b200moe {
@@ -252,6 +256,140 @@ __global__ void __launch_bounds__(256) combine_rows(const __grid_constant__ Comb
   }
 }
 
+// Batches of prefill size: persistent CTAs stream each token's K expert rows (and its
+// shared-expert row) into a ring of shared-memory stages with bulk copies that complete
+// on the stage's mbarrier.  Warp 8 issues the copies; warps 0-7 reduce each token from
+// shared memory in combine_body's order, so both kernels give the same bits.  A CTA
+// keeps up to kCombineStageBudget bytes of row reads in flight without holding them in
+// registers (the warp kernel is bound by the loads each warp can keep outstanding).
+constexpr int CB_CONSUMERS = 256;
+constexpr int CB_THREADS = CB_CONSUMERS + 32;
+constexpr uint32_t kCombineStageBudget = 96 * 1024;
+constexpr int kCombineMaxStages = 8;
+constexpr int kCombineBulkMinT = 2048;
+
+template <typename E>
+__device__ __forceinline__ void lds8(const uint8_t* p, float (&v)[8]) {
+  if constexpr (sizeof(E) == 2) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+template <typename E, bool PEER, int KT>
+__global__ void __launch_bounds__(CB_THREADS) combine_rows_bulk(const __grid_constant__ CombineParams p, int stages) {
+  extern __shared__ __align__(128) uint8_t cb_rows[];  // [stages][K (+1 shared)][H]
+  __shared__ uint64_t full[kCombineMaxStages], empty[kCombineMaxStages];
+  __shared__ int s_abort;
+  __shared__ uint32_t s_target;
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rb = static_cast<uint32_t>(p.H) * sizeof(E);
+  const uint32_t stage_bytes = rb * static_cast<uint32_t>(p.K + (p.shared ? 1 : 0));
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CB_CONSUMERS / 32);
+    }
+    fence_mbar_init();
+    s_abort = 0;
+  }
+  pdl_trigger();
+  pdl_wait();
+  if (PEER && threadIdx.x == 0) {
+    const uint32_t target = *p.wait_expect + 1u;
+    bool ok = true;
+    for (int d = 0; d < p.wait_n && ok; ++d) ok = wait_flag_geq(p.wait_flags + d, target, p.wait_timeout_ns, p.status);
+    if (!ok) record_status(p.status, kStatusTimeout);
+    s_target = target;
+  }
+  __syncthreads();
+  int issued = 0;  // producer: stages filled so far
+  if (warp == CB_CONSUMERS / 32) {
+    if (lane == 0) {
+      if (PEER) fence_proxy_async_global();  // rows the peers stored, acquired above
+      const E* y = static_cast<const E*>(p.y);
+      const E* sh = static_cast<const E*>(p.shared);
+      int& i = issued;
+      for (int t = blockIdx.x; t < p.T; t += gridDim.x, ++i) {
+        const int s = i % stages;
+        const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, &s_abort, p.status)) break;
+        uint8_t* dst = cb_rows + static_cast<size_t>(s) * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        for (int k = 0; k < p.K; ++k) {
+          const int row = p.pos_of[static_cast<int64_t>(t) * p.K + k];
+          bulk_load(dst + k * rb, y + static_cast<int64_t>(row) * p.ldy, rb, &full[s]);
+        }
+        if (sh) bulk_load(dst + p.K * rb, sh + static_cast<int64_t>(t) * p.lds, rb, &full[s]);
+      }
+    }
+  } else {
+    int i = 0;
+    for (int t = blockIdx.x; t < p.T; t += gridDim.x, ++i) {
+      const int s = i % stages;
+      const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
+      float wts[KT];
+#pragma unroll
+      for (int k = 0; k < KT; ++k) wts[k] = (k < p.K) ? p.topk_w[static_cast<int64_t>(t) * p.K + k] : 0.f;
+      const float g = (p.shared && p.shared_gate) ? p.shared_gate[t] : 1.f;
+      if (!mbar_wait(&full[s], ph, &s_abort, p.status)) break;
+      const uint8_t* src = cb_rows + static_cast<size_t>(s) * stage_bytes;
+      E* out = static_cast<E*>(p.out) + static_cast<int64_t>(t) * p.ldo;
+      for (int c = threadIdx.x * 8; c < p.H; c += CB_CONSUMERS * 8) {
+        float v[KT][8];
+#pragma unroll
+        for (int k = 0; k < KT; ++k)
+          if (k < p.K) lds8<E>(src + k * rb + c * sizeof(E), v[k]);
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+          if (k < p.K) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = fmaf(wts[k], v[k][e], acc[e]);
+          }
+        }
+        if (p.shared) {
+          float sv[8];
+          lds8<E>(src + p.K * rb + c * sizeof(E), sv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = fmaf(g, sv[e], acc[e]);
+        }
+        store8<E>(out + c, acc);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  __syncthreads();
+  if (s_abort && warp == CB_CONSUMERS / 32 && lane == 0) {
+    // a wait gave up: the copies already issued land before the CTA exits
+    volatile int no_abort = 0;
+    for (int j = max(0, issued - stages); j < issued; ++j)
+      mbar_wait(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u, &no_abort, p.status);
+  }
+  if (PEER) {
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = (atomicAdd(p.wait_ticket, 1u) == gridDim.x - 1);
+    __syncthreads();
+    if (s_last && threadIdx.x == 0) {
+      *p.wait_expect = s_target;
+      *p.wait_ticket = 0u;
+    }
+  }
+}
+
 int launch_permute(const PermuteParams& p, cudaStream_t stream) {
   const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t);
   if (p.peer_mode)  // always launched: a rank without tokens still publishes empty counts
@@ -273,9 +411,72 @@ static cudaError_t launch_combine_k(const CombineParams& p, int grid, cudaStream
   return launch_kernel(combine_rows<E, PEER, 8>, dim3(grid), dim3(256), 0, stream, p);
 }
 
+template <typename E, bool PEER>
+static cudaError_t launch_combine_bulk_k(const CombineParams& p, int grid, int stages, size_t smem,
+                                         cudaStream_t stream) {
+  if (p.K <= 2) return launch_kernel(combine_rows_bulk<E, PEER, 2>, dim3(grid), dim3(CB_THREADS), smem, stream, p, stages);
+  if (p.K <= 4) return launch_kernel(combine_rows_bulk<E, PEER, 4>, dim3(grid), dim3(CB_THREADS), smem, stream, p, stages);
+  if (p.K <= 6) return launch_kernel(combine_rows_bulk<E, PEER, 6>, dim3(grid), dim3(CB_THREADS), smem, stream, p, stages);
+  return launch_kernel(combine_rows_bulk<E, PEER, 8>, dim3(grid), dim3(CB_THREADS), smem, stream, p, stages);
+}
+
+template <typename E, bool PEER>
+static bool set_combine_bulk_smem() {
+  const int bytes = static_cast<int>(kCombineStageBudget);
+  return cudaFuncSetAttribute(combine_rows_bulk<E, PEER, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
+         cudaFuncSetAttribute(combine_rows_bulk<E, PEER, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
+         cudaFuncSetAttribute(combine_rows_bulk<E, PEER, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
+         cudaFuncSetAttribute(combine_rows_bulk<E, PEER, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+}
+
+// Stages of the bulk kernel for this shape (0: the shape does not fit two stages).
+static int combine_bulk_stages(const CombineParams& p) {
+  const size_t eb = p.dtype == kDtypeBF16 ? 2 : 4;
+  const size_t stage = static_cast<size_t>(p.H) * eb * static_cast<size_t>(p.K + (p.shared ? 1 : 0));
+  const int stages = static_cast<int>(min64(kCombineMaxStages, static_cast<int64_t>(kCombineStageBudget / stage)));
+  return stages >= 2 ? stages : 0;
+}
+
+// B200MOE_COMBINE=warp|bulk forces a combine kernel (tests and tuning); otherwise
+// the bulk kernel runs from kCombineBulkMinT tokens when the shape fits its stages.
+static bool use_combine_bulk(const CombineParams& p) {
+  if (combine_bulk_stages(p) == 0) return false;
+  const char* v = getenv("B200MOE_COMBINE");
+  if (v != nullptr && strcmp(v, "warp") == 0) return false;
+  if (v != nullptr && strcmp(v, "bulk") == 0) return true;
+  return p.T >= kCombineBulkMinT;
+}
+
+static int launch_combine_bulk(const CombineParams& p, bool peer, cudaStream_t stream) {
+  static std::atomic<uint64_t> attr_set_mask{0};  // one bit per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set_mask.load(std::memory_order_acquire) & bit)) {
+    if (!set_combine_bulk_smem<__nv_bfloat16, false>() || !set_combine_bulk_smem<__nv_bfloat16, true>() ||
+        !set_combine_bulk_smem<float, false>() || !set_combine_bulk_smem<float, true>())
+      return -3;
+    attr_set_mask.fetch_or(bit, std::memory_order_release);
+  }
+  const int stages = combine_bulk_stages(p);
+  const size_t eb = p.dtype == kDtypeBF16 ? 2 : 4;
+  const size_t smem = static_cast<size_t>(stages) * static_cast<size_t>(p.H) * eb * (p.K + (p.shared ? 1 : 0));
+  // two CTAs per SM (2 x 96 KB of stages), one token per CTA at least
+  const int grid = static_cast<int>(max64(1, min64(p.T, 2 * static_cast<int64_t>(num_sms()))));
+  cudaError_t e;
+  if (p.dtype == kDtypeBF16)
+    e = peer ? launch_combine_bulk_k<__nv_bfloat16, true>(p, grid, stages, smem, stream)
+             : launch_combine_bulk_k<__nv_bfloat16, false>(p, grid, stages, smem, stream);
+  else
+    e = peer ? launch_combine_bulk_k<float, true>(p, grid, stages, smem, stream)
+             : launch_combine_bulk_k<float, false>(p, grid, stages, smem, stream);
+  return e == cudaSuccess ? 0 : -2;
+}
+
 int launch_combine(const CombineParams& p, cudaStream_t stream) {
   const bool peer = p.wait_n > 0;
   if (p.T == 0 && !peer) return 0;  // peer mode always runs: it consumes the arrival flags
+  if (use_combine_bulk(p)) return launch_combine_bulk(p, peer, stream);
   const int64_t warps = static_cast<int64_t>(p.T) * ((p.H + 255) / 256);
   const int grid = static_cast<int>(max64(1, (warps * 32 + 255) / 256));
   cudaError_t e;

@@ -232,6 +232,37 @@ def test_combine_matches_fp32_reference(cuda_device, dtype, K):
     assert max_rel(out, ref) < tol
 
 
+@pytest.mark.parametrize("T,K,H,dtype,shared,gate", [
+    (3000, 2, 4096, torch.bfloat16, False, False),   # Mixtral prefill shape (fewer tokens)
+    (2500, 6, 2048, torch.bfloat16, True, False),    # DeepSeek-V2-Lite: shared experts, no gate
+    (2100, 4, 2048, torch.bfloat16, True, True),     # Qwen1.5: gated shared expert
+    (2049, 8, 1024, torch.float32, False, False),
+    (5, 1, 512, torch.bfloat16, True, True),          # fewer tokens than CTAs
+    (700, 3, 7168, torch.bfloat16, False, False),     # two stages of 43 KB
+])
+def test_combine_bulk_and_warp_kernels_agree(cuda_device, monkeypatch, T, K, H, dtype, shared, gate):
+    """The bulk-copy combine (prefill sizes) and the warp combine reduce in the same
+    order: bit-identical outputs; both within the fp32 reference's tolerance."""
+    g = torch.Generator().manual_seed(T + K)
+    y = torch.randn(T * K, H, generator=g).to(dtype)
+    pos = torch.randperm(T * K, generator=g).view(T, K).to(torch.int32)
+    w = torch.rand(T, K, generator=g)
+    sh = torch.randn(T, H, generator=g).to(dtype) if shared else None
+    sg = torch.rand(T, generator=g) if gate else None
+    d = lambda t: None if t is None else t.to(cuda_device)
+    outs = {}
+    for variant in ("warp", "bulk"):
+        monkeypatch.setenv("B200MOE_COMBINE", variant)
+        outs[variant] = ops.combine(d(y), d(pos), d(w), shared=d(sh), shared_gate=d(sg))
+    torch.cuda.synchronize()
+    assert torch.equal(outs["warp"], outs["bulk"])
+    ref = (w[:, :, None] * y.float()[pos.long()]).sum(1)
+    if shared:
+        ref = ref + (sg[:, None] if gate else 1.0) * sh.float()
+    tol = 4e-3 if dtype == torch.bfloat16 else 1e-6
+    assert max_rel(outs["bulk"], ref) < tol
+
+
 def test_gather_segments_and_inverse_map(cuda_device):
     H = 64
     src = torch.randn(50, H).to(torch.bfloat16)
@@ -406,7 +437,11 @@ def test_small_batch_fused_sigmoid_router(cuda_device, T):
 
 
 @pytest.mark.parametrize("T,E,K,slots", [(136, 128, 8, 128), (256, 128, 8, 160), (1000, 64, 6, 64),
-                                         (4096, 128, 8, 128), (20000, 8, 2, 8), (40000, 16, 4, 16)])
+                                         (4096, 128, 8, 128), (20000, 8, 2, 8), (40000, 16, 4, 16),
+                                         # 1024 token blocks (four column chunks); every
+                                         # experts-per-lane width of the selection
+                                         (65536, 33, 4, 33), (3000, 32, 8, 32), (3000, 256, 8, 256),
+                                         (5000, 200, 6, 230)])
 def test_selection_and_permute_order_at_many_token_blocks(cuda_device, T, E, K, slots):
     """Token-block counts from 17 to 1024 (every column-scan shape of the selection's
     last CTA): ids, slot counts and offsets, and the permute order equal the oracle's
