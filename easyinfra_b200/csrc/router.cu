@@ -233,31 +233,57 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
   return va > vb || (va == vb && ia < ib);
 }
 
+// Unsigned key with the order of the float (-0 taken as +0): key(a) > key(b) <=> a > b.
+__device__ __forceinline__ uint32_t order_key(float v) {
+  uint32_t b = __float_as_uint(v);
+  if (b == 0x80000000u) b = 0u;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Warp-wide maximum of a float (redux.sync, sm_100a); exact, so order-independent.
+__device__ __forceinline__ float warp_max_f32(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
 // One warp per token of [t_begin, t_end): selection, weights, replica pick and the
 // CTA's slot histogram (hist, shared, zeroed by the caller; the scoring-1 scratch
-// follows it).  Shared by router_select and the fused small-batch router.
+// follows it).  Shared by router_select and the fused small-batch router.  NJ =
+// ceil(E / 32) experts per lane (compile time, so loops cover only live experts); the
+// next token's logits are loaded before the current token is processed.
+template <int NJ>
 __device__ __forceinline__ void select_tokens(const RouterSelectParams& p, int t_begin, int t_end,
                                               int32_t* hist) {
   float* cbuf = reinterpret_cast<float*>(hist + p.num_slots) + (threadIdx.x >> 5) * 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = t_begin + warp; t < t_end; t += blockDim.x >> 5) {
+  const int step = blockDim.x >> 5;
+  float nxt[NJ];
+  auto load_logits = [&](int t) {
     const float* lg = p.logits + static_cast<int64_t>(t) * p.E1;
-    float v[RS_MAXJ];     // selection key per owned expert
-    float sc[RS_MAXJ];    // value reported as the routing weight (before renorm)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int e = lane + 32 * j;
+      nxt[j] = (e < p.E) ? lg[e] : -INFINITY;
+    }
+  };
+  if (t_begin + warp < t_end) load_logits(t_begin + warp);
+  for (int t = t_begin + warp; t < t_end; t += step) {
+    const float* lg = p.logits + static_cast<int64_t>(t) * p.E1;
+    float v[NJ];     // selection key per owned expert
+    float sc[NJ];    // value reported as the routing weight (before renorm)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) v[j] = nxt[j];
+    if (t + step < t_end) load_logits(t + step);
     if (p.scoring == 0) {
       // softmax over the experts (fp32), select on the probabilities
       float m = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < RS_MAXJ; ++j) {
-        const int e = lane + 32 * j;
-        v[j] = (e < p.E) ? lg[e] : -INFINITY;
-        m = fmaxf(m, v[j]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      for (int j = 0; j < NJ; ++j) m = fmaxf(m, v[j]);
+      m = warp_max_f32(m);
       float s = 0.f;
 #pragma unroll
-      for (int j = 0; j < RS_MAXJ; ++j) {
+      for (int j = 0; j < NJ; ++j) {
         const int e = lane + 32 * j;
         v[j] = (e < p.E) ? expf(v[j] - m) : 0.f;
         s += v[j];
@@ -265,7 +291,7 @@ __device__ __forceinline__ void select_tokens(const RouterSelectParams& p, int t
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
 #pragma unroll
-      for (int j = 0; j < RS_MAXJ; ++j) {
+      for (int j = 0; j < NJ; ++j) {
         v[j] = (lane + 32 * j < p.E) ? v[j] / s : -1.f;
         sc[j] = v[j];
       }
@@ -274,10 +300,10 @@ __device__ __forceinline__ void select_tokens(const RouterSelectParams& p, int t
       // with the largest sum of their two best choices; others' choices become 0.0
       const int gs = p.E / p.n_group;
 #pragma unroll
-      for (int j = 0; j < RS_MAXJ; ++j) {
+      for (int j = 0; j < NJ; ++j) {
         const int e = lane + 32 * j;
         if (e < p.E) {
-          sc[j] = 1.f / (1.f + expf(-lg[e]));
+          sc[j] = 1.f / (1.f + expf(-v[j]));
           v[j] = sc[j] + p.correction_bias[e];
           cbuf[e] = v[j];
         } else {
@@ -309,59 +335,53 @@ __device__ __forceinline__ void select_tokens(const RouterSelectParams& p, int t
         if (bi < 32) keep |= 1u << bi;
       }
 #pragma unroll
-      for (int j = 0; j < RS_MAXJ; ++j) {
+      for (int j = 0; j < NJ; ++j) {
         const int e = lane + 32 * j;
         if (e < p.E && !((keep >> (e / gs)) & 1u)) v[j] = 0.f;
       }
       __syncwarp();
     }
 
-    // top-k: K rounds of a warp arg-max on (key desc, expert asc); the winner's
-    // reported value (probability, or sigmoid score) travels with it.
-    float selp[8];
-    int sele[8];
+    // top-k: K rounds of a warp arg-max on (key desc, expert asc): each lane offers its
+    // best untaken expert, one redux picks the largest key and a second the lowest
+    // expert holding it; the winner's reported value (probability, or sigmoid score)
+    // comes from its lane.  Lane k keeps round k's result.
     uint32_t taken = 0;
+    float denom = 0.f, wk = 0.f;
+    int ek = 0;
     for (int k = 0; k < p.K; ++k) {
-      float bv = -INFINITY, bs = 0.f;
-      int bi = 0x7fffffff;
+      uint32_t bkey = 0;  // 0: no candidate (below the key of every float but NaN)
+      int bj = -1;
+      float bs = 0.f;
 #pragma unroll
-      for (int j = 0; j < RS_MAXJ; ++j) {
+      for (int j = 0; j < NJ; ++j) {
         const int e = lane + 32 * j;
-        if (e < p.E && !((taken >> j) & 1u) && better(v[j], e, bv, bi)) {
-          bv = v[j];
-          bs = sc[j];
-          bi = e;
+        if (e < p.E && !((taken >> j) & 1u)) {
+          const uint32_t kj = order_key(v[j]);
+          if (bj < 0 || kj > bkey) {  // strict: ties keep the lower expert
+            bkey = kj;
+            bj = j;
+            bs = sc[j];
+          }
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (better(ov, oi, bv, bi)) {
-          bv = ov;
-          bs = os;
-          bi = oi;
-        }
+      const uint32_t mkey = __reduce_max_sync(0xffffffffu, bkey);
+      const uint32_t cand = (bj >= 0 && bkey == mkey) ? static_cast<uint32_t>(lane + 32 * bj) : 0xffffffffu;
+      const int win = static_cast<int>(__reduce_min_sync(0xffffffffu, cand));
+      const float ws = __shfl_sync(0xffffffffu, bs, win & 31);
+      if ((win & 31) == lane) taken |= 1u << (win >> 5);
+      if (k == lane) {
+        wk = ws;
+        ek = win;
       }
-      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-      selp[k] = bs;
-      sele[k] = bi;
+      denom += ws;
     }
-    float denom = 1.f;
     if (p.renorm) {
-      denom = 0.f;
-      for (int k = 0; k < p.K; ++k) denom += selp[k];
       if (p.scoring == 1) denom += 1e-20f;
+    } else {
+      denom = 1.f;
     }
     if (lane < p.K) {
-      float wk = 0.f;
-      int ek = 0;
-      for (int k = 0; k < p.K; ++k)
-        if (k == lane) {
-          wk = selp[k];
-          ek = sele[k];
-        }
       if (p.renorm) wk = wk / denom;
       wk *= p.scale;
       if (p.round_bf16) wk = bf16_round(wk);
@@ -388,71 +408,91 @@ __device__ __forceinline__ void select_tokens(const RouterSelectParams& p, int t
   }
 }
 
+// select_tokens for the expert count in p (NJ from E).
+__device__ __forceinline__ void select_tokens_any(const RouterSelectParams& p, int t_begin, int t_end,
+                                                  int32_t* hist) {
+  if (p.E <= 32)
+    select_tokens<1>(p, t_begin, t_end, hist);
+  else if (p.E <= 64)
+    select_tokens<2>(p, t_begin, t_end, hist);
+  else if (p.E <= 128)
+    select_tokens<4>(p, t_begin, t_end, hist);
+  else
+    select_tokens<RS_MAXJ>(p, t_begin, t_end, hist);
+}
+
 // Column pass of the last CTA over block_counts [num_slots][nb]: WRITE == false sums
 // each slot's column into hist[slot]; WRITE == true replaces the column by absolute
 // write offsets (exclusive prefix from the slot offset in hist).  SB slots per warp
-// iteration, each lane owning per_lane <= PL contiguous blocks; every load of an
-// iteration is issued before any arithmetic, so a warp has SB * PL loads in flight
-// instead of one per slot.
+// iteration; a column is walked in chunks of 32 * PL blocks, each lane owning PL
+// contiguous blocks of a chunk, with a carry between chunks.  Every load of a chunk
+// is issued before any arithmetic, so a warp has SB * PL loads in flight.
 template <int SB, int PL, bool WRITE>
 __device__ __forceinline__ void slot_columns(const RouterSelectParams& p, int32_t* hist, int nb) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
-  const int per_lane = (nb + 31) / 32;
   for (int s0 = warp * SB; s0 < p.num_slots; s0 += nwarps * SB) {
-    int v[SB][PL];
+    int carry[SB];
 #pragma unroll
-    for (int i = 0; i < SB; ++i) {
+    for (int i = 0; i < SB; ++i) carry[i] = (WRITE && s0 + i < p.num_slots) ? hist[s0 + i] : 0;
+    for (int b0 = 0; b0 < nb; b0 += 32 * PL) {
+      int v[SB][PL];
 #pragma unroll
-      for (int k = 0; k < PL; ++k) {
-        const int b = lane * per_lane + k;
-        v[i][k] = (k < per_lane && b < nb && s0 + i < p.num_slots)
-                      ? __ldcg(p.block_counts + static_cast<int64_t>(s0 + i) * nb + b)
-                      : 0;
-      }
-    }
+      for (int i = 0; i < SB; ++i) {
 #pragma unroll
-    for (int i = 0; i < SB; ++i) {
-      int part = 0;
-#pragma unroll
-      for (int k = 0; k < PL; ++k) part += v[i][k];
-      if (!WRITE) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        if (lane == 0 && s0 + i < p.num_slots) hist[s0 + i] = part;
-      } else {
-        int incl = part;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int n = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += n;
+        for (int k = 0; k < PL; ++k) {
+          const int b = b0 + lane * PL + k;
+          v[i][k] = (b < nb && s0 + i < p.num_slots)
+                        ? __ldcg(p.block_counts + static_cast<int64_t>(s0 + i) * nb + b)
+                        : 0;
         }
-        if (s0 + i < p.num_slots) {
-          int32_t* col = p.block_counts + static_cast<int64_t>(s0 + i) * nb;
-          int run = hist[s0 + i] + incl - part;
+      }
 #pragma unroll
-          for (int k = 0; k < PL; ++k) {
-            const int b = lane * per_lane + k;
-            if (k < per_lane && b < nb) {
-              col[b] = run;
-              run += v[i][k];
+      for (int i = 0; i < SB; ++i) {
+        int part = 0;
+#pragma unroll
+        for (int k = 0; k < PL; ++k) part += v[i][k];
+        if (!WRITE) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+          carry[i] += part;
+        } else {
+          int incl = part;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+          }
+          if (s0 + i < p.num_slots) {
+            int32_t* col = p.block_counts + static_cast<int64_t>(s0 + i) * nb;
+            int run = carry[i] + incl - part;
+#pragma unroll
+            for (int k = 0; k < PL; ++k) {
+              const int b = b0 + lane * PL + k;
+              if (b < nb) {
+                col[b] = run;
+                run += v[i][k];
+              }
             }
           }
+          carry[i] += __shfl_sync(0xffffffffu, incl, 31);
         }
       }
+    }
+    if (!WRITE && lane == 0) {
+#pragma unroll
+      for (int i = 0; i < SB; ++i)
+        if (s0 + i < p.num_slots) hist[s0 + i] = carry[i];
     }
   }
 }
 
 template <bool WRITE>
 __device__ __forceinline__ void slot_columns_any(const RouterSelectParams& p, int32_t* hist, int nb) {
-  const int per_lane = (nb + 31) / 32;
-  if (per_lane <= 2)
+  if (nb <= 64)
     slot_columns<8, 2, WRITE>(p, hist, nb);
-  else if (per_lane <= 8)
-    slot_columns<4, 8, WRITE>(p, hist, nb);
   else
-    slot_columns<1, 32, WRITE>(p, hist, nb);  // nb <= 1024 (checked on the host)
+    slot_columns<2, 8, WRITE>(p, hist, nb);  // chunks of 256 blocks
 }
 
 // Run by every thread of the CTA that arrived last, once every CTA's histogram is in
@@ -520,7 +560,8 @@ __device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32
   if (threadIdx.x == 0) *p.ticket = 0u;
 }
 
-__global__ void __launch_bounds__(256) router_select(const __grid_constant__ RouterSelectParams p) {
+template <int NJ>
+__global__ void __launch_bounds__(256, 4) router_select(const __grid_constant__ RouterSelectParams p) {
   extern __shared__ int32_t hist[];  // [num_slots], then (scoring 1) 8 warps x 256 floats
   __shared__ int s_last;
   pdl_trigger();
@@ -528,7 +569,7 @@ __global__ void __launch_bounds__(256) router_select(const __grid_constant__ Rou
   for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) hist[s] = 0;
   __syncthreads();
   const int t_begin = blockIdx.x * p.tb;
-  select_tokens(p, t_begin, min(p.T, t_begin + p.tb), hist);
+  select_tokens<NJ>(p, t_begin, min(p.T, t_begin + p.tb), hist);
   __syncthreads();
   for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x)
     p.block_counts[static_cast<int64_t>(s) * p.nblocks + blockIdx.x] = hist[s];
@@ -631,7 +672,7 @@ __global__ void __launch_bounds__(256) router_small_fused(const __grid_constant_
   __threadfence();
   for (int s = threadIdx.x; s < sp.num_slots; s += blockDim.x) hist[s] = 0;
   __syncthreads();
-  select_tokens(sp, 0, T, hist);
+  select_tokens_any(sp, 0, T, hist);
   __syncthreads();
   for (int s = threadIdx.x; s < sp.num_slots; s += blockDim.x) sp.block_counts[s] = hist[s];  // one block
   __threadfence();
@@ -738,7 +779,15 @@ int launch_router_select(const RouterSelectParams& p, cudaStream_t stream) {
   if (p.T == 0) return 0;
   const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t) +
                       (p.scoring == 1 ? 8 * 256 * sizeof(float) : 0);
-  launch_kernel(router_select, dim3(p.nblocks), dim3(256), smem, stream, p);
+  const dim3 grid(p.nblocks);
+  if (p.E <= 32)
+    launch_kernel(router_select<1>, grid, dim3(256), smem, stream, p);
+  else if (p.E <= 64)
+    launch_kernel(router_select<2>, grid, dim3(256), smem, stream, p);
+  else if (p.E <= 128)
+    launch_kernel(router_select<4>, grid, dim3(256), smem, stream, p);
+  else
+    launch_kernel(router_select<RS_MAXJ>, grid, dim3(256), smem, stream, p);
   return 0;
 }
 
