@@ -142,7 +142,7 @@ __device__ __forceinline__ int clamp_run(int cnt, int run, int64_t cap) {
 __device__ __forceinline__ bool last_cta(uint32_t* ticket, int* s_last) {
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) *s_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+  if (threadIdx.x == 0) *s_last = (atomicAdd(ticket, 1u) == gridDim.x * gridDim.y * gridDim.z - 1);
   __syncthreads();
   return *s_last != 0;
 }

@@ -39,7 +39,8 @@ __global__ void __launch_bounds__(256) permute_rows(const __grid_constant__ Perm
   pdl_trigger();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (PEER && blockIdx.x == 0 && threadIdx.x < p.ep.G) ep_publish_meta(p.ep, p.slot_offsets, threadIdx.x);
+  if (PEER && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < p.ep.G)
+    ep_publish_meta(p.ep, p.slot_offsets, threadIdx.x);
   const int t0 = blockIdx.x * p.tb;
   const int nt = min(p.tb, p.T - t0);
   const int ne = nt * p.K;
@@ -71,9 +72,11 @@ __global__ void __launch_bounds__(256) permute_rows(const __grid_constant__ Perm
 
   for (int i = threadIdx.x; i < ne; i += blockDim.x) {
     const int d = pos[i];
-    p.pos_of[flat0 + i] = d;
-    if (p.send_token) p.send_token[d] = t0 + i / p.K;
-    if (p.send_slot) p.send_slot[d] = i % p.K;
+    if (blockIdx.y == 0) {
+      p.pos_of[flat0 + i] = d;
+      if (p.send_token) p.send_token[d] = t0 + i / p.K;
+      if (p.send_slot) p.send_slot[d] = i % p.K;
+    }
     if (PEER) {
       // send row d of slot s -> row (rank * cap + j) of the owner's receive region,
       // j = d - (first send row of the owner rank)
@@ -91,13 +94,18 @@ __global__ void __launch_bounds__(256) permute_rows(const __grid_constant__ Perm
   if (PEER) __syncthreads();
 
   // Row copies: one warp per token; the token row is read once (PM_BATCH 16-byte loads
-  // per lane in flight together) and written K times.
+  // per lane in flight together) and written K times.  Small batches split the columns
+  // over gridDim.y CTAs per token block (CTA y copies its slice of every row), so a few
+  // token blocks still spread over many SMs.
   constexpr int PM_BATCH = 8;
-  const int vec_per_row = p.row_bytes / 16;
+  const int vec_total = p.row_bytes / 16;
+  const int vec_slice = (vec_total + gridDim.y - 1) / gridDim.y;
+  const int vec_begin = blockIdx.y * vec_slice;
+  const int vec_per_row = min(vec_total, vec_begin + vec_slice);
   for (int lt = warp; lt < nt; lt += blockDim.x >> 5) {
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.x) +
                                                       static_cast<int64_t>(t0 + lt) * p.x_stride);
-    for (int v0 = 0; v0 < vec_per_row; v0 += PM_BATCH * 32) {
+    for (int v0 = vec_begin; v0 < vec_per_row; v0 += PM_BATCH * 32) {
       uint4 val[PM_BATCH];
 #pragma unroll
       for (int u = 0; u < PM_BATCH; ++u) {
@@ -390,15 +398,25 @@ __global__ void __launch_bounds__(CB_THREADS) combine_rows_bulk(const __grid_con
   }
 }
 
+// Column slices per token block: enough CTAs for about two per SM, each slice at least
+// one 512-byte batch of a warp's 16-byte copies.
+static int permute_slices(const PermuteParams& p, int nblocks) {
+  const int by_sms = (2 * num_sms() + nblocks - 1) / nblocks;
+  const int by_row = max64(1, p.row_bytes / 512);
+  return static_cast<int>(max64(1, min64(by_sms, by_row)));
+}
+
 int launch_permute(const PermuteParams& p, cudaStream_t stream) {
   const size_t smem = static_cast<size_t>(p.num_slots) * sizeof(int32_t);
-  if (p.peer_mode)  // always launched: a rank without tokens still publishes empty counts
-    return launch_kernel(permute_rows<true>, dim3(p.nblocks > 0 ? p.nblocks : 1), dim3(256), smem, stream, p) ==
+  if (p.peer_mode) {  // always launched: a rank without tokens still publishes empty counts
+    const int nb = p.nblocks > 0 ? p.nblocks : 1;
+    return launch_kernel(permute_rows<true>, dim3(nb, permute_slices(p, nb)), dim3(256), smem, stream, p) ==
                    cudaSuccess
                ? 0
                : -2;
+  }
   if (p.T == 0) return 0;
-  launch_kernel(permute_rows<false>, dim3(p.nblocks), dim3(256), smem, stream, p);
+  launch_kernel(permute_rows<false>, dim3(p.nblocks, permute_slices(p, p.nblocks)), dim3(256), smem, stream, p);
   return 0;
 }
 
