@@ -105,6 +105,11 @@ int gemm_variant_from_env() {
 }
 
 constexpr size_t kTicketBytes = 256;
+constexpr int kMaxSlots = 8192;
+constexpr size_t kTotalsBytes = kMaxSlots * sizeof(int32_t);
+// Counters at the start of a router workspace that must be zero before a call (every
+// call leaves them zero again).
+constexpr size_t kCounterBytes = kTicketBytes + kTotalsBytes;
 
 int tokens_per_block(int T) {
   if (T > 32768) return 64;  // at most 1024 token blocks up to 65536 tokens
@@ -122,6 +127,7 @@ size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 struct RouterWs {
   uint32_t* ticket;
+  int32_t* slot_totals;
   int32_t* block_counts;
   float* logits;
   size_t bytes;
@@ -133,6 +139,8 @@ RouterWs router_ws_layout(void* base, int T, int E1, int num_slots) {
   size_t off = 0;
   w.ticket = reinterpret_cast<uint32_t*>(p);
   off += kTicketBytes;
+  w.slot_totals = reinterpret_cast<int32_t*>(p + off);  // fixed place and size: always zero between calls
+  off += kTotalsBytes;
   w.block_counts = reinterpret_cast<int32_t*>(p + off);
   off += align256(static_cast<size_t>(num_slots) * nblocks_for(T) * sizeof(int32_t));
   w.logits = reinterpret_cast<float*>(p + off);
@@ -183,6 +191,7 @@ int select_common(const float* logits, int has_shared_gate, int T, int E, int K,
   s.phys_ids = phys_ids;
   s.shared_gate = shared_gate;
   s.block_counts = ws.block_counts;
+  s.slot_totals = ws.slot_totals;
   s.slot_counts = slot_counts;
   s.slot_offsets = slot_offsets;
   s.ticket = ws.ticket;
@@ -205,7 +214,7 @@ int check_select_args(int T, int E, int K, int num_slots, const int32_t* log2phy
   if (T > 65536) return fail(B200MOE_EUNSUPPORTED, "T=%d above 65536 tokens per call", T);
   if (E < 1 || E > 256) return fail(B200MOE_EUNSUPPORTED, "E=%d outside [1, 256]", E);
   if (K < 1 || K > 8 || K > E) return fail(B200MOE_EUNSUPPORTED, "K=%d outside [1, min(8, E)]", K);
-  if (num_slots < 1 || num_slots > 8192) return fail(B200MOE_EUNSUPPORTED, "num_slots=%d", num_slots);
+  if (num_slots < 1 || num_slots > kMaxSlots) return fail(B200MOE_EUNSUPPORTED, "num_slots=%d", num_slots);
   if ((log2phy == nullptr) != (rep_count == nullptr))
     return fail(B200MOE_EINVAL, "log2phy and rep_count must both be given or both be NULL");
   if (log2phy == nullptr && num_slots < E)
@@ -1094,7 +1103,7 @@ extern "C" int b200moe_router_noalloc(const void* x, int64_t ldx, int x_dtype, c
   if (rc) return rc;
   // The completion counter must read zero when the kernels start; a call that was cut
   // short could have left it set, so clear it on the caller's stream every time.
-  const cudaError_t e = cudaMemsetAsync(ws, 0, kTicketBytes, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = cudaMemsetAsync(ws, 0, kCounterBytes, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(B200MOE_ECUDA, "clearing the router scratch counter: %s", cudaGetErrorString(e));
   return b200moe_router(x, ldx, x_dtype, gate_w, gate_bias, has_shared_gate, T, H, E, K, renorm, scale,
                         log2phy, rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate,

@@ -35,6 +35,7 @@ struct RouterSelectParams {
   int32_t* phys_ids;     // [T, K]
   float* shared_gate;    // [T] sigmoid(shared-gate logit), when has_shared_gate
   int32_t* block_counts; // [num_slots, nblocks]  -> becomes absolute write offsets
+  int32_t* slot_totals;  // [num_slots], zero between calls (nblocks > 16: CTAs add their counts)
   int32_t* slot_counts;  // [num_slots]
   int32_t* slot_offsets; // [num_slots + 1]
   uint32_t* ticket;      // zero before the first call; the last CTA resets it

@@ -421,20 +421,19 @@ __device__ __forceinline__ void select_tokens_any(const RouterSelectParams& p, i
     select_tokens<RS_MAXJ>(p, t_begin, t_end, hist);
 }
 
-// Column pass of the last CTA over block_counts [num_slots][nb]: WRITE == false sums
-// each slot's column into hist[slot]; WRITE == true replaces the column by absolute
-// write offsets (exclusive prefix from the slot offset in hist).  SB slots per warp
-// iteration; a column is walked in chunks of 32 * PL blocks, each lane owning PL
-// contiguous blocks of a chunk, with a carry between chunks.  Every load of a chunk
-// is issued before any arithmetic, so a warp has SB * PL loads in flight.
-template <int SB, int PL, bool WRITE>
-__device__ __forceinline__ void slot_columns(const RouterSelectParams& p, int32_t* hist, int nb) {
+// Column pass of the last CTA over block_counts [num_slots][nb]: each slot's column
+// becomes absolute write offsets (exclusive prefix from the slot offset in hist).  SB
+// slots per warp iteration; a column is walked in chunks of 32 * PL blocks, each lane
+// owning PL contiguous blocks of a chunk, with a carry between chunks.  Every load of a
+// chunk is issued before any arithmetic, so a warp has SB * PL loads in flight.
+template <int SB, int PL>
+__device__ __forceinline__ void slot_columns(const RouterSelectParams& p, const int32_t* hist, int nb) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   for (int s0 = warp * SB; s0 < p.num_slots; s0 += nwarps * SB) {
     int carry[SB];
 #pragma unroll
-    for (int i = 0; i < SB; ++i) carry[i] = (WRITE && s0 + i < p.num_slots) ? hist[s0 + i] : 0;
+    for (int i = 0; i < SB; ++i) carry[i] = (s0 + i < p.num_slots) ? hist[s0 + i] : 0;
     for (int b0 = 0; b0 < nb; b0 += 32 * PL) {
       int v[SB][PL];
 #pragma unroll
@@ -452,59 +451,56 @@ __device__ __forceinline__ void slot_columns(const RouterSelectParams& p, int32_
         int part = 0;
 #pragma unroll
         for (int k = 0; k < PL; ++k) part += v[i][k];
-        if (!WRITE) {
+        int incl = part;
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-          carry[i] += part;
-        } else {
-          int incl = part;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int n = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += n;
+        }
+        if (s0 + i < p.num_slots) {
+          int32_t* col = p.block_counts + static_cast<int64_t>(s0 + i) * nb;
+          int run = carry[i] + incl - part;
 #pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int n = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += n;
-          }
-          if (s0 + i < p.num_slots) {
-            int32_t* col = p.block_counts + static_cast<int64_t>(s0 + i) * nb;
-            int run = carry[i] + incl - part;
-#pragma unroll
-            for (int k = 0; k < PL; ++k) {
-              const int b = b0 + lane * PL + k;
-              if (b < nb) {
-                col[b] = run;
-                run += v[i][k];
-              }
+          for (int k = 0; k < PL; ++k) {
+            const int b = b0 + lane * PL + k;
+            if (b < nb) {
+              col[b] = run;
+              run += v[i][k];
             }
           }
-          carry[i] += __shfl_sync(0xffffffffu, incl, 31);
         }
+        carry[i] += __shfl_sync(0xffffffffu, incl, 31);
       }
-    }
-    if (!WRITE && lane == 0) {
-#pragma unroll
-      for (int i = 0; i < SB; ++i)
-        if (s0 + i < p.num_slots) hist[s0 + i] = carry[i];
     }
   }
 }
 
-template <bool WRITE>
-__device__ __forceinline__ void slot_columns_any(const RouterSelectParams& p, int32_t* hist, int nb) {
+__device__ __forceinline__ void slot_columns_any(const RouterSelectParams& p, const int32_t* hist, int nb) {
   if (nb <= 64)
-    slot_columns<8, 2, WRITE>(p, hist, nb);
+    slot_columns<8, 2>(p, hist, nb);
   else
-    slot_columns<2, 8, WRITE>(p, hist, nb);  // chunks of 256 blocks
+    slot_columns<2, 8>(p, hist, nb);  // chunks of 256 blocks
 }
+
+// Up to this many token blocks the last CTA sums each slot's column itself (one load
+// round trip); above it every CTA also adds its histogram into slot_totals.
+constexpr int kSmallNb = 16;
 
 // Run by every thread of the CTA that arrived last, once every CTA's histogram is in
 // block_counts: slot totals, slot offsets, absolute per-(slot, block) offsets; resets
-// the ticket.  hist is shared scratch of num_slots ints.
+// the ticket (and slot_totals).  hist is shared scratch of num_slots ints.
 __device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32_t* hist) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // ---- last CTA: slot totals, slot offsets, absolute per-(slot, block) offsets.
   __threadfence();
   const int nb = p.nblocks;
-  constexpr int kSmallNb = 16;
-  if (nb <= kSmallNb) {
+  if (nb > kSmallNb) {
+    // every CTA added its histogram into slot_totals: one round trip, then reset
+    for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) {
+      hist[s] = __ldcg(p.slot_totals + s);
+      p.slot_totals[s] = 0;
+    }
+  } else {
     // few blocks (decode batches): one thread per slot, one round trip of loads
     for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) {
       const int32_t* col = p.block_counts + static_cast<int64_t>(s) * nb;
@@ -514,8 +510,6 @@ __device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32
         if (b < nb) tot += __ldcg(col + b);
       hist[s] = tot;
     }
-  } else {
-    slot_columns_any<false>(p, hist, nb);
   }
   __syncthreads();
   if (warp == 0) {
@@ -555,7 +549,7 @@ __device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32
         }
     }
   } else {
-    slot_columns_any<true>(p, hist, nb);
+    slot_columns_any(p, hist, nb);
   }
   if (threadIdx.x == 0) *p.ticket = 0u;
 }
@@ -571,8 +565,11 @@ __global__ void __launch_bounds__(256, 4) router_select(const __grid_constant__ 
   const int t_begin = blockIdx.x * p.tb;
   select_tokens<NJ>(p, t_begin, min(p.T, t_begin + p.tb), hist);
   __syncthreads();
-  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x)
-    p.block_counts[static_cast<int64_t>(s) * p.nblocks + blockIdx.x] = hist[s];
+  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) {
+    const int c = hist[s];
+    p.block_counts[static_cast<int64_t>(s) * p.nblocks + blockIdx.x] = c;
+    if (p.nblocks > kSmallNb && c != 0) atomicAdd(p.slot_totals + s, c);  // order-free integer sum
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = (atomicAdd(p.ticket, 1u) == static_cast<uint32_t>(p.nblocks - 1));

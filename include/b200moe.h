@@ -67,9 +67,10 @@ B200MOE_API const char* b200moe_last_error(void);
 B200MOE_API int b200moe_tokens_per_block(int T);
 
 /* Bytes of workspace b200moe_router / b200moe_permute need for T tokens, E1 router
- * columns and num_slots physical slots.  The first 256 bytes hold a completion
- * counter that must be zero before the first call on a workspace; every call leaves
- * it zero again, so zero the workspace once at allocation. */
+ * columns and num_slots physical slots.  The first 256 + 32768 bytes hold counters
+ * (a completion ticket and per-slot totals) that must be zero before the first call
+ * on a workspace; every call leaves them zero again, so zero the workspace once at
+ * allocation. */
 B200MOE_API size_t b200moe_router_workspace_bytes(int T, int E1, int num_slots);
 
 /*
