@@ -207,7 +207,9 @@ def test_peer_exchange_with_prefill_gemm_kernels(cuda_device, name, variant, mon
             xg.close()
 
 
-@pytest.mark.parametrize("name,T", [("mixtral_g2", 640), ("dsv2_g2", 1400)])
+@pytest.mark.parametrize("name,T", [("mixtral_g2", 640), ("dsv2_g2", 1400),
+                                    # >= 2048 tokens per rank: the bulk-copy combine in peer mode
+                                    ("mixtral_g2", 2304), ("dsv2_g2", 2100)])
 def test_peer_exchange_receive_region_gemms(cuda_device, name, T):
     """Prefill-sized batches: the CTA-pair GEMMs read the receive region per (source,
     slot) segment (no regroup copy) and wait per source; the layer equals the NCCL
