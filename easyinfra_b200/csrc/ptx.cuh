@@ -332,6 +332,16 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16_f32(int M, int N) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Pull `bytes` of read-only data (weights written at load time, never by the previous
+// kernel) toward L2 before griddepcontrol.wait, so the kernel's first reads of it after
+// the wait hit L2 instead of waiting on HBM.  One prefetch per 128-byte line, spread
+// over the CTA's threads.
+__device__ __forceinline__ void prefetch_l2_lines(const void* base, int64_t bytes) {
+  const char* b = static_cast<const char*>(base);
+  for (int64_t off = static_cast<int64_t>(threadIdx.x) * 128; off < bytes; off += static_cast<int64_t>(blockDim.x) * 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(b + off));
+}
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));

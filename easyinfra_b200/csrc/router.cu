@@ -149,6 +149,8 @@ template <typename E>
 __global__ void __launch_bounds__(256) router_logits_gemv(RouterLogitsParams p) {
   __shared__ float red[8][RG];
   pdl_trigger();
+  prefetch_l2_lines(static_cast<const E*>(p.w) + static_cast<int64_t>(blockIdx.y) * p.H,
+                    static_cast<int64_t>(p.H) * sizeof(E));  // weights: before the wait
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.y, t0 = blockIdx.x * RG;
@@ -482,6 +484,41 @@ __device__ __forceinline__ void slot_columns_any(const RouterSelectParams& p, co
     slot_columns<2, 8>(p, hist, nb);  // chunks of 256 blocks
 }
 
+// Exclusive scan of the slot totals in hist (warp 0): writes slot_counts and
+// slot_offsets; hist[] becomes the slot offsets.
+__device__ __forceinline__ void scan_slot_totals(const RouterSelectParams& p, int32_t* hist) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp != 0) return;
+  int run = 0;
+  for (int base = 0; base < p.num_slots; base += 32) {
+    const int s = base + lane;
+    const int c = (s < p.num_slots) ? hist[s] : 0;
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (s < p.num_slots) {
+      p.slot_counts[s] = c;
+      p.slot_offsets[s] = run + incl - c;
+      hist[s] = run + incl - c;
+    }
+    run += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) p.slot_offsets[p.num_slots] = run;
+}
+
+// One token block (the fused small-batch router): its histogram in hist already holds
+// the slot totals and its write offsets are the slot offsets — no round trip through
+// block_counts.  Called by every thread after a __syncthreads.
+__device__ __forceinline__ void select_finish_one_block(const RouterSelectParams& p, int32_t* hist) {
+  scan_slot_totals(p, hist);
+  __syncthreads();
+  for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) p.block_counts[s] = hist[s];
+  if (threadIdx.x == 0) *p.ticket = 0u;
+}
+
 // Up to this many token blocks the last CTA sums each slot's column itself (one load
 // round trip); above it every CTA also adds its histogram into slot_totals.
 constexpr int kSmallNb = 16;
@@ -512,27 +549,7 @@ __device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32
     }
   }
   __syncthreads();
-  if (warp == 0) {
-    // exclusive scan of the slot totals; hist[] becomes the slot offsets
-    int run = 0;
-    for (int base = 0; base < p.num_slots; base += 32) {
-      const int s = base + lane;
-      const int c = (s < p.num_slots) ? hist[s] : 0;
-      int incl = c;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
-      }
-      if (s < p.num_slots) {
-        p.slot_counts[s] = c;
-        p.slot_offsets[s] = run + incl - c;
-        hist[s] = run + incl - c;
-      }
-      run += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) p.slot_offsets[p.num_slots] = run;
-  }
+  scan_slot_totals(p, hist);
   __syncthreads();
   if (nb <= kSmallNb) {
     for (int s = threadIdx.x; s < p.num_slots; s += blockDim.x) {
@@ -599,6 +616,11 @@ __global__ void __launch_bounds__(256) router_small_fused(const __grid_constant_
   __shared__ float nred[NORM_THREADS / 32];
   __shared__ int s_last;
   pdl_trigger();
+  // the router row and the norm weight are model weights: fetch them toward L2 while
+  // the previous kernel finishes
+  prefetch_l2_lines(static_cast<const E*>(lp.w) + static_cast<int64_t>(blockIdx.x) * lp.H,
+                    static_cast<int64_t>(lp.H) * sizeof(E));
+  if (has_norm) prefetch_l2_lines(np.weight, static_cast<int64_t>(np.H) * sizeof(E));
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
@@ -671,10 +693,7 @@ __global__ void __launch_bounds__(256) router_small_fused(const __grid_constant_
   __syncthreads();
   select_tokens_any(sp, 0, T, hist);
   __syncthreads();
-  for (int s = threadIdx.x; s < sp.num_slots; s += blockDim.x) sp.block_counts[s] = hist[s];  // one block
-  __threadfence();
-  __syncthreads();
-  select_finish(sp, hist);
+  select_finish_one_block(sp, hist);
 }
 
 size_t router_small_fused_smem(int T, int H, int x_dtype, int num_slots, int scoring) {
