@@ -19,7 +19,8 @@ template <typename E>
 __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(const __grid_constant__ AddNormParams p) {
   __shared__ float red[NORM_THREADS / 32];
   pdl_trigger();
-  prefetch_l2_lines(p.weight, static_cast<int64_t>(p.H) * sizeof(E));  // weights: before the wait
+  // the norm weight toward L2 before the wait (one CTA: L2 is shared by all)
+  if (blockIdx.x == 0) prefetch_l2_lines(p.weight, static_cast<int64_t>(p.H) * sizeof(E));
   pdl_wait();
   const int64_t t = blockIdx.x;
   E* rout = static_cast<E*>(p.residual_out) + t * p.ld;

@@ -149,8 +149,9 @@ template <typename E>
 __global__ void __launch_bounds__(256) router_logits_gemv(RouterLogitsParams p) {
   __shared__ float red[8][RG];
   pdl_trigger();
-  prefetch_l2_lines(static_cast<const E*>(p.w) + static_cast<int64_t>(blockIdx.y) * p.H,
-                    static_cast<int64_t>(p.H) * sizeof(E));  // weights: before the wait
+  if (blockIdx.x == 0)  // this column's router row toward L2 before the wait (once per column)
+    prefetch_l2_lines(static_cast<const E*>(p.w) + static_cast<int64_t>(blockIdx.y) * p.H,
+                      static_cast<int64_t>(p.H) * sizeof(E));
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.y, t0 = blockIdx.x * RG;
@@ -527,7 +528,6 @@ constexpr int kSmallNb = 16;
 // block_counts: slot totals, slot offsets, absolute per-(slot, block) offsets; resets
 // the ticket (and slot_totals).  hist is shared scratch of num_slots ints.
 __device__ __forceinline__ void select_finish(const RouterSelectParams& p, int32_t* hist) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // ---- last CTA: slot totals, slot offsets, absolute per-(slot, block) offsets.
   __threadfence();
   const int nb = p.nblocks;
@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(256) router_small_fused(const __grid_constant_
   // the previous kernel finishes
   prefetch_l2_lines(static_cast<const E*>(lp.w) + static_cast<int64_t>(blockIdx.x) * lp.H,
                     static_cast<int64_t>(lp.H) * sizeof(E));
-  if (has_norm) prefetch_l2_lines(np.weight, static_cast<int64_t>(np.H) * sizeof(E));
+  if (has_norm && blockIdx.x == 0) prefetch_l2_lines(np.weight, static_cast<int64_t>(np.H) * sizeof(E));
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x;
