@@ -92,7 +92,7 @@ int check_launch(const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// B200MOE_GEMM_VARIANT=token|token_small|weight|pair forces one grouped-GEMM kernel
+// B200MOE_GEMM_VARIANT=token|token_small|weight|weight_wide|pair forces one grouped-GEMM kernel
 // (tuning and tests); unset or "auto" picks by rows per slot.
 int gemm_variant_from_env() {
   const char* v = getenv("B200MOE_GEMM_VARIANT");
@@ -100,6 +100,7 @@ int gemm_variant_from_env() {
   if (strcmp(v, "token") == 0) return kGemmTokenMajor;
   if (strcmp(v, "token_small") == 0) return kGemmTokenMajorSmallM;
   if (strcmp(v, "weight") == 0) return kGemmWeightMajor;
+  if (strcmp(v, "weight_wide") == 0) return kGemmWeightMajorWide;
   if (strcmp(v, "pair") == 0) return kGemmTokenMajorPair;
   return kGemmAuto;
 }

@@ -390,7 +390,8 @@ static bool pair_regime(const GemmLaunch& L) {
 int launch_grouped_swiglu(const GemmLaunch& L, cudaStream_t stream) {
   if (L.p.P > GM_MAXP) return -4;
   const int v = L.variant;
-  if (v == kGemmWeightMajor || (v == kGemmAuto && decode_regime(L))) return launch_grouped_wm(L, true, stream);
+  if (v == kGemmWeightMajor || v == kGemmWeightMajorWide || (v == kGemmAuto && decode_regime(L)))
+    return launch_grouped_wm(L, true, v == kGemmAuto ? -1 : (v == kGemmWeightMajorWide ? 1 : 0), stream);
   if (v == kGemmTokenMajorSmallM) return run_gemm<64, 9, true, 32>(L, stream);
   if ((v == kGemmTokenMajorPair || (v == kGemmAuto && pair_regime(L))) && pair_gemm_supported(L, true))
     return launch_grouped_pair(L, true, stream);
@@ -400,7 +401,8 @@ int launch_grouped_swiglu(const GemmLaunch& L, cudaStream_t stream) {
 int launch_grouped_down(const GemmLaunch& L, cudaStream_t stream) {
   if (L.p.P > GM_MAXP) return -4;
   const int v = L.variant;
-  if (v == kGemmWeightMajor || (v == kGemmAuto && decode_regime(L))) return launch_grouped_wm(L, false, stream);
+  if (v == kGemmWeightMajor || v == kGemmWeightMajorWide || (v == kGemmAuto && decode_regime(L)))
+    return launch_grouped_wm(L, false, v == kGemmAuto ? -1 : (v == kGemmWeightMajorWide ? 1 : 0), stream);
   if (v == kGemmTokenMajorSmallM) return run_gemm<64, 9, false, 32>(L, stream);
   if ((v == kGemmTokenMajorPair || (v == kGemmAuto && pair_regime(L))) && pair_gemm_supported(L, false))
     return launch_grouped_pair(L, false, stream);

@@ -299,6 +299,7 @@ enum GemmVariant : int {
   kGemmTokenMajorSmallM = 2,  // 32 token rows per tile, N = 64
   kGemmWeightMajor = 3,       // M = 128 weight rows x N = 32 tokens (decode)
   kGemmTokenMajorPair = 4,    // CTA pairs: M = 256 token rows x N = 256 (cta_group::2)
+  kGemmWeightMajorWide = 5,   // weight-major with up to 64-token tiles for slots above 32 rows
 };
 
 struct GemmLaunch {
@@ -315,7 +316,8 @@ struct GemmLaunch {
 // 128-byte swizzle.  Returns 0 on success.
 int make_tma_map_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
                     int box_rows);
-int launch_grouped_wm(const GemmLaunch& L, bool swiglu, cudaStream_t stream);
+// wide: 0 = 32-token tiles, 1 = up to 64-token tiles for slots above 32 rows, -1 = by rows per slot
+int launch_grouped_wm(const GemmLaunch& L, bool swiglu, int wide, cudaStream_t stream);
 bool pair_gemm_supported(const GemmLaunch& L, bool swiglu);
 int launch_grouped_pair(const GemmLaunch& L, bool swiglu, cudaStream_t stream);
 

@@ -181,7 +181,7 @@ def _gemm_ref(x, wgu, wd, offs):
     ([1000, 17], 1024, 512),
     ([0, 0, 3], 128, 64),
 ])
-@pytest.mark.parametrize("variant", ["auto", "token", "token_small", "weight", "pair"])
+@pytest.mark.parametrize("variant", ["auto", "token", "token_small", "weight", "weight_wide", "pair"])
 def test_grouped_gemms_match_fp32_reference(cuda_device, counts, H, I, variant, monkeypatch):
     """Every grouped-GEMM kernel variant on every shape (auto = the regime's choice)."""
     monkeypatch.setenv("B200MOE_GEMM_VARIANT", variant)
@@ -198,7 +198,7 @@ def test_grouped_gemms_match_fp32_reference(cuda_device, counts, H, I, variant, 
     assert max_rel(y, y_ref) < TIGHT_TOL, max_rel(y, y_ref)
 
 
-@pytest.mark.parametrize("variant", ["token", "token_small", "weight", "pair"])
+@pytest.mark.parametrize("variant", ["token", "token_small", "weight", "weight_wide", "pair"])
 def test_grouped_down_row_scatter(cuda_device, variant, monkeypatch):
     monkeypatch.setenv("B200MOE_GEMM_VARIANT", variant)
     counts, H, I = [70, 0, 200], 256, 128
