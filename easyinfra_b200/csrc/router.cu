@@ -10,15 +10,21 @@
 //   phys = log2phy[e][(t*K + k) % replica_count[e]]  (blocks/moe/base.py:40-64)
 // and the per-slot token histogram (blocks/moe/base.py:343-364).
 //
-// Three launches:
-//   router_logits_bf16  one warp per 16 tokens, mma.sync m16n8k16 bf16 -> fp32,
-//                       logits rounded to bf16 exactly like F.linear's bf16 output.
+// Kernels (a logits kernel, then the selection; one fused launch up to 8 tokens):
+//   router_logits_bf16  T > 256: one warp per 16 tokens, mma.sync m16n8k16 bf16 ->
+//                       fp32 on a cp.async ring; logits rounded to bf16 exactly like
+//                       F.linear's bf16 output.
+//   router_logits_gemv  T <= 256: one CTA per (8 tokens, router column), fixed-order
+//                       reduction.
 //   router_logits_f32   SIMT fp32 dot products (fp32 activations).
 //   router_select       one warp per token: fp32 softmax, top-k with ties broken to
-//                       the lowest expert index, renorm, scaling, dtype rounding,
-//                       replica pick, per-block slot histogram; the last CTA to
-//                       finish turns the histograms into slot counts, slot offsets
-//                       and per-(slot, block) write offsets for the permute kernel.
+//                       the lowest expert index (warp reductions), renorm, scaling,
+//                       dtype rounding, replica pick, per-block slot histogram; the
+//                       last CTA to finish turns the histograms into slot counts,
+//                       slot offsets and per-(slot, block) write offsets for the
+//                       permute kernel.
+//   router_small_fused  T <= 8: optional residual add + RMSNorm, the GEMV logits and
+//                       the selection in one launch, with the bits of the kernels above.
 #include <cstdlib>
 
 #include <atomic>
