@@ -194,7 +194,30 @@ class B200MoeAll2AllBlock(nn.Module):
                                            self.post_attention_layernorm.weight,
                                            self.post_attention_layernorm.variance_epsilon)
         st = self.layer().route_and_permute(normed)
+        if self.ep_size == 1:
+            # no exchange: the split bookkeeping happens here, on the compute stream that
+            # produced the counts (the dispatch stage's communicate function runs on the
+            # comm stream, which no event orders after this stage when EP size is 1)
+            self._local_splits(chunk, st, residual.device)
         chunk.active_variables = (st, normed if self.has_shared else None, residual)
+
+    def _local_splits(self, chunk, st, device):
+        P = self.num_physical_experts
+        c = st.route.slot_counts.view(1, 1, P).cpu()
+        st.send_splits = [int(c.sum())]
+        st.recv_splits = st.send_splits
+        self._set_count_attributes(chunk, st, c, device)
+
+    def _set_count_attributes(self, chunk, st, c, device):
+        """The chunk attributes the reference's dispatch leaves for the scheduler and
+        the balancer (moe_all2all.py:397-445)."""
+        chunk.global_tok_all_expert_count_2d_cpu = c
+        chunk.global_tok_device_count_cpu = c.sum((0, -1))
+        chunk.global_tok_local_ep_rank_count = c[:, self.ep_rank, :].sum(-1)
+        chunk.global_tok_local_expert_count_2d_flat_list = c[:, self.ep_rank, :].reshape(-1).tolist()
+        chunk.send_token_split = st.send_splits
+        chunk.recv_token_split = st.recv_splits
+        chunk.global_tok_device_count = chunk.global_tok_device_count_cpu.to(device, non_blocking=True)
 
     def all2all_moe_dispatch_communicate(self, chunk):
         """Count all-gather, host split lists, token all-to-all (moe_all2all.py:375-459)."""
@@ -206,17 +229,7 @@ class B200MoeAll2AllBlock(nn.Module):
             lay.plan_exchange(st, counts)
             lay.dispatch(st)
             c = torch.from_numpy(counts).view(G, G, P)
-        else:
-            c = st.route.slot_counts.view(1, 1, P).cpu()
-            st.send_splits = [int(c.sum())]
-            st.recv_splits = st.send_splits
-        chunk.global_tok_all_expert_count_2d_cpu = c
-        chunk.global_tok_device_count_cpu = c.sum((0, -1))
-        chunk.global_tok_local_ep_rank_count = c[:, self.ep_rank, :].sum(-1)
-        chunk.global_tok_local_expert_count_2d_flat_list = c[:, self.ep_rank, :].reshape(-1).tolist()
-        chunk.send_token_split = st.send_splits
-        chunk.recv_token_split = st.recv_splits
-        chunk.global_tok_device_count = chunk.global_tok_device_count_cpu.to(residual.device, non_blocking=True)
+            self._set_count_attributes(chunk, st, c, residual.device)
         chunk.comm_handler = None
         chunk.compute_wait_comm = False
         chunk.active_variables = (st, normed, residual)

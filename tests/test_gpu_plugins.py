@@ -86,6 +86,95 @@ def test_block_stages_ep1_match_oracle(cuda_device):
     assert max_rel(res_out, exp_res) < TIGHT_TOL
 
 
+class _ChunkDriver:
+    """ChunkBlock's stream/event protocol (easyinfra/schedule/chunk.py:204-269), restated
+    for the test: compute functions run on a compute stream and communicate functions on
+    a comm stream; a stage with communication records compute_event after its compute
+    function, and its communicate function waits on it and records comm_event; the next
+    compute waits on comm_event unless the communicate function cleared
+    chunk.compute_wait_comm, in which case the wait moves to the next compute that
+    follows a communicating stage."""
+
+    def __init__(self, blk, chunk_id, residual, hidden, compute_stream, comm_stream):
+        self.blk = blk
+        self.chunk = NS(chunk_id=chunk_id, active_variables=(residual, hidden), compute_wait_comm=True)
+        self.compute_stream, self.comm_stream = compute_stream, comm_stream
+        self.compute_event, self.comm_event = torch.cuda.Event(), torch.cuda.Event()
+        self.n_compute = self.n_comm = 0
+        self.skipped_comm = False
+
+    def run_compute(self):
+        i = self.n_compute
+        _, compute, _ = self.blk.stages[i]
+        has = self.blk.stage_has_communication
+        last_has = i > 0 and has[i - 1]
+        with torch.cuda.stream(self.compute_stream):
+            if self.chunk.compute_wait_comm:
+                if last_has or self.skipped_comm:
+                    self.compute_stream.wait_event(self.comm_event)
+                    self.skipped_comm = False
+            elif last_has:
+                self.skipped_comm = True
+            compute(self.chunk)
+            if has[i]:
+                self.compute_event.record()
+        self.chunk.compute_wait_comm = True
+        self.n_compute += 1
+
+    def run_communicate(self):
+        i = self.n_comm
+        _, _, comm = self.blk.stages[i]
+        with torch.cuda.stream(self.comm_stream):
+            if self.blk.stage_has_communication[i]:
+                self.comm_stream.wait_event(self.compute_event)
+            comm(self.chunk)
+            if self.blk.stage_has_communication[i]:
+                self.comm_event.record()
+        self.n_comm += 1
+
+
+def test_block_two_streams_two_chunks_match_oracle(cuda_device):
+    """The block under ChunkBlock's two-stream protocol with two chunks interleaved stage
+    by stage (compute of both, then communicate of both): each chunk's residual and
+    output equal the oracle's.  At EP size 1 no stage has communication, so nothing
+    orders the comm stream after compute; the block keeps every device read on the
+    compute stream."""
+    shape = C.small(C.CONFIGS["qwen3"], hidden=256, intermediate=128)
+    E, H, I = shape.num_experts, shape.hidden, shape.intermediate
+    g1 = NS(group_size=1, local_rank=0)
+    blk = B200MoeAll2AllBlock(0, H, I, "silu", False, False, E, shape.top_k, shape.norm_topk_prob, False,
+                              None, g1, g1, False, device=cuda_device)
+    gw = C.router_weight(shape, 0)
+    wgu, wd = C.expert_weights(shape, 0, list(range(E)))
+    with torch.no_grad():
+        blk.gate.weight.copy_(gw)
+        blk.experts.experts_gate_up_weight.copy_(wgu)
+        blk.experts.experts_down_weight.copy_(wd)
+    compute_stream, comm_stream = torch.cuda.Stream(cuda_device), torch.cuda.Stream(cuda_device)
+    inputs, drivers = [], []
+    for cid, T in enumerate((48, 5)):
+        res = C.hidden_states(shape, T, seed_offset=10 + cid)
+        hid = C.hidden_states(shape, T, seed_offset=20 + cid)
+        inputs.append((res, hid))
+        drivers.append(_ChunkDriver(blk, cid, res.to(cuda_device), hid.to(cuda_device), compute_stream,
+                                    comm_stream))
+    torch.cuda.synchronize()
+    for _ in range(len(blk.stages)):
+        for d in drivers:
+            d.run_compute()
+        for d in drivers:
+            d.run_communicate()
+    torch.cuda.synchronize()
+    for (res, hid), d in zip(inputs, drivers):
+        res_out, hid_out = d.chunk.active_variables
+        r, normed = O.add_rmsnorm(res, hid, torch.ones(H, dtype=res.dtype), 1e-6)
+        tr = O.moe_layer_ep([normed], O.LayerWeights(gw, wgu, wd), shape.top_k, shape.norm_topk_prob,
+                            torch.arange(E).view(1, E), use_eplb=False, fp32_accumulate=True)[0]
+        assert d.chunk.send_token_split == [res.shape[0] * shape.top_k]
+        assert torch.equal(res_out.cpu(), r)
+        assert max_rel(hid_out, tr.out_f32) < TIGHT_TOL
+
+
 def test_cutlass_grouped_gemm_single_op(cuda_device):
     """torch.ops.ops.cutlass_grouped_gemm_single(A, B_list, block_sizes) with the weight
     list repeated once per source rank, as SingleGroupGEMMMoE calls it."""
