@@ -326,7 +326,12 @@ __global__ void __launch_bounds__(CB_THREADS) combine_rows_bulk(const __grid_con
   int issued = 0;  // producer: stages filled so far
   if (warp == CB_CONSUMERS / 32) {
     if (lane == 0) {
-      if (PEER) fence_proxy_async_global();  // rows the peers stored, acquired above
+      if (PEER) {
+        // rows the peers stored: acquire their flags in this thread too (thread 0 saw
+        // them reach the target; they only grow), then order the bulk reads after it
+        for (int d = 0; d < p.wait_n; ++d) (void)ld_acquire_sys(p.wait_flags + d);
+        fence_proxy_async_global();
+      }
       const E* y = static_cast<const E*>(p.y);
       const E* sh = static_cast<const E*>(p.shared);
       int& i = issued;
