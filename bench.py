@@ -26,6 +26,7 @@ import statistics
 import subprocess
 import sys
 import time
+from typing import Optional
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
@@ -47,7 +48,9 @@ WORKLOADS = {
     "qwen3-decode-b256": ("qwen3", "decode", 256),
 }
 DEFAULT_WORKLOAD = "mixtral-prefill"
-SECONDARY = {"mixtral-prefill": ["mixtral-decode"]}
+# measured after the main workload of a default run, each on its own stack
+SECONDARY = {"mixtral-prefill": ["mixtral-decode", "qwen15-decode", "dsv2lite-prefill", "qwen3-decode-b1",
+                                 "qwen3-decode-b16", "qwen3-decode-b64", "qwen3-decode-b256"]}
 
 
 def parse_args():
@@ -118,7 +121,14 @@ def cpu_sample(cfg_key: str, tokens: int, target_s: float = 3.0, layer: int = 0)
 
 
 def run_reference(args):
+    """The reference arm: the reference's eager MoE path (restated by the oracle) on the
+    host cores, one layer per step on a bounded token sample of the workload.  Its
+    `config` is the GPU arm's for the same workload and GPU count; `layers_timed`
+    says that one layer of the stack is timed (the metric is per MoE layer)."""
+    from easyinfra_b200 import configs as C
     cfg_key, phase, tokens = WORKLOADS[args.workload]
+    shape = C.CONFIGS[cfg_key]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     n, _, sample, cores, run = cpu_sample(cfg_key, tokens)
     for _ in range(args.warmup):
         run(n)
@@ -129,7 +139,8 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.workload, "tokens_per_rank": tokens, "phase": phase},
+        "config": config_dict(shape, args.workload, args.layers or shape.num_layers, world, args.transport),
+        "layers_timed": 1,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -213,7 +224,29 @@ def build_stack(cfg_key, rank, world, device, group, n_layers):
     return shape, layers
 
 
+def config_dict(shape, workload: str, n_layers: int, world: int, transport: Optional[str]):
+    """The `config` of a bench line (both arms print the same dict for one workload)."""
+    return {"workload": f"{shape.name} {workload} stack", "layers": n_layers,
+            "tokens_per_rank": WORKLOADS[workload][2], "hidden": shape.hidden,
+            "experts": shape.num_experts, "top_k": shape.top_k, "intermediate": shape.intermediate,
+            "parallelism": f"ep{world}", "transport": None if world == 1 else transport,
+            "l2": "inputs larger than L2 (per-layer weights "
+                  f"{3 * shape.hidden * shape.intermediate * 2 * shape.num_experts / 1e9:.2f} GB)"}
+
+
+def workload_groups(args):
+    """[(config key, [workloads])]: the main workload's configuration first, then the
+    secondary workloads grouped by configuration (one stack built per configuration)."""
+    wls = [args.workload] + ([] if args.no_secondary else SECONDARY.get(args.workload, []))
+    groups = {}
+    for w in wls:
+        groups.setdefault(WORKLOADS[w][0], []).append(w)
+    return list(groups.items())
+
+
 def run_ours(args):
+    import gc
+
     import torch.distributed as dist
     from easyinfra_b200 import build, ops
     from easyinfra_b200 import configs as C
@@ -231,25 +264,8 @@ def run_ours(args):
         from easyinfra_b200.communicator import GroupCommunicator
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
         group = GroupCommunicator(group=dist.group.WORLD)
-    cfg_key, phase, tokens = WORKLOADS[args.workload]
-    shape = C.CONFIGS[cfg_key]
-    n_layers = args.layers or shape.num_layers
-    shape, layers = build_stack(cfg_key, rank, world, device, group, n_layers)
     hbm, bf16_burst, bf16_sus, peak_kind = peaks()
-    xg = None
     xg_status = torch.zeros(1, dtype=torch.int32, device=device)
-    if world > 1 and args.transport.startswith("nvlink"):
-        from easyinfra_b200.peer_exchange import PeerExchange
-        wls = [args.workload] + ([] if args.no_secondary else SECONDARY.get(args.workload, []))
-        max_t = max(WORKLOADS[w][2] for w in wls if WORKLOADS[w][0] == cfg_key)
-        lay0 = layers[0]
-        xg = PeerExchange.create(group, rank=rank, world_size=world, slots_per_rank=lay0.P, hidden=lay0.H,
-                                 inter=lay0.I, dtype=shape.dtype, max_tokens=max_t, top_k=shape.top_k,
-                                 device=device, timeout_s=10.0, status=xg_status,
-                                 fused=args.transport == "nvlink")
-        for lay in layers:
-            lay.exchange = xg
-    use_graph = world == 1 or xg is not None
 
     def barrier():
         if world > 1:
@@ -262,9 +278,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    results = {}
-
-    def measure(wl_name, with_roofline):
+    def measure(wl_name, shape, layers, use_graph, with_roofline):
         from easyinfra_b200.stack import MoEStack
         cfg_key_w, phase_w, T = WORKLOADS[wl_name]
         x = C.hidden_states(shape, T, rank=rank, device=device)
@@ -390,23 +404,56 @@ def run_ours(args):
                                    "hit_slots_mean": statistics.mean(layer_hit)}
         return res
 
-    main = measure(args.workload, with_roofline=True)
+    main = None
+    main_shape = main_layers = None
     secondary = []
-    if not args.no_secondary:
-        for wl in SECONDARY.get(args.workload, []):
-            if WORKLOADS[wl][0] == cfg_key:
-                s = measure(wl, with_roofline=True)
-                secondary.append({k: s[k] for k in ("workload", "value", "ms", "e2e_value", "graph") if k in s}
-                                 | ({"roofline": s["roofline"]} if "roofline" in s else {}))
+    exchange_status = 0
+    for cfg_key, wls in workload_groups(args):
+        shape = C.CONFIGS[cfg_key]
+        n_layers = args.layers or shape.num_layers
+        shape, layers = build_stack(cfg_key, rank, world, device, group, n_layers)
+        xg = None
+        if world > 1 and args.transport.startswith("nvlink"):
+            from easyinfra_b200.peer_exchange import PeerExchange
+            lay0 = layers[0]
+            xg = PeerExchange.create(group, rank=rank, world_size=world, slots_per_rank=lay0.P, hidden=lay0.H,
+                                     inter=lay0.I, dtype=shape.dtype, max_tokens=max(WORKLOADS[w][2] for w in wls),
+                                     top_k=shape.top_k, device=device, timeout_s=10.0, status=xg_status,
+                                     fused=args.transport == "nvlink")
+            for lay in layers:
+                lay.exchange = xg
+        use_graph = world == 1 or xg is not None
+        for wl in wls:
+            r = measure(wl, shape, layers, use_graph, with_roofline=True)
+            if wl == args.workload:
+                main, main_shape, main_layers = r, shape, len(layers)
+                continue
+            secondary.append({k: r[k] for k in ("workload", "value", "ms", "e2e_value", "graph", "launches")
+                              if k in r}
+                             | {"config": config_dict(shape, wl, len(layers), world, args.transport)}
+                             | ({"roofline": r["roofline"]} if "roofline" in r else {})
+                             | ({"clocks": r["clocks"]} if r.get("clocks") else {}))
+        if xg is not None:
+            exchange_status = max(exchange_status, int(max_over_ranks(float(xg_status.item()))))
+            if cfg_key == WORKLOADS[args.workload][0] and not args.no_secondary:
+                # the reference's own exchange on the same stack: count all-gather, one host
+                # sync and NCCL all_to_all_single each way (moe_all2all.py:97-173, :272-289)
+                for lay in layers:
+                    lay.exchange = None
+                r = measure(args.workload, shape, layers, False, with_roofline=False)
+                secondary.append({k: r[k] for k in ("workload", "value", "ms", "e2e_value", "graph", "launches")}
+                                 | {"config": config_dict(shape, args.workload, len(layers), world, "nccl")})
+            xg.close(group)
+        del layers, xg
+        gc.collect()
+        torch.cuda.empty_cache()
+    cfg_key, phase, tokens = WORKLOADS[args.workload]
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         n, _, sample, cores, run = cpu_sample(cfg_key, tokens)
         ts = [run(n) for _ in range(3)]
         cpu = {"value": n / statistics.median(ts), "unit": UNIT, "cores": cores, "kind": "port",
                "sample": sample}
-    exchange_status = int(max_over_ranks(float(xg_status.item()))) if world > 1 else 0
-    if xg is not None:
-        xg.close(group)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -416,12 +463,7 @@ def run_ours(args):
         "metric": METRIC, "value": main["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": main["ms"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{shape.name} {args.workload} stack", "layers": len(layers),
-                   "tokens_per_rank": main["T"], "hidden": shape.hidden, "experts": shape.num_experts,
-                   "top_k": shape.top_k, "intermediate": shape.intermediate,
-                   "parallelism": f"ep{world}",
-                   "transport": None if world == 1 else args.transport, "l2": "inputs larger than L2 (per-layer weights "
-                   f"{3 * shape.hidden * shape.intermediate * 2 * shape.num_experts / 1e9:.2f} GB)"},
+        "config": config_dict(main_shape, args.workload, main_layers, world, args.transport),
         "e2e": {"value": main["e2e_value"], "unit": UNIT, "h2d_bytes_per_step": main["h2d"],
                 "d2h_bytes_per_step": main["d2h"], "ms_per_step": main["e2e_ms"]},
         "gpu_launches": main["launches"],

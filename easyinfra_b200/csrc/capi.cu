@@ -36,6 +36,14 @@ int num_sms() {
   return n;
 }
 
+int gemm_grid_limit() {
+  const int n = num_sms();
+  const char* v = getenv("B200MOE_GEMM_MAX_CTAS");
+  if (v == nullptr) return n;
+  const int cap = atoi(v);
+  return (cap >= 2 && cap < n) ? cap : n;
+}
+
 // ------------------------------------------------------------------ segment gather
 __global__ void __launch_bounds__(256) gather_segments_kernel(const uint8_t* src, uint8_t* dst,
                                                               int64_t row_bytes,
@@ -1061,22 +1069,43 @@ namespace {
 
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[64] = {nullptr};
+CUcontext g_scratch_ctx[64] = {nullptr};
 
-// Device address of g_router_scratch on the current device.  Looked up once per
-// device (with that device current), on the first call there.  In host code the
-// symbol itself is only a host-side stand-in, never a device address.
+// The calling thread's current CUDA context (driver entry point, no libcuda link).
+CUcontext current_context() {
+  using Fn = CUresult (*)(CUcontext*);
+  static const Fn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<Fn>(p);
+    return static_cast<Fn>(nullptr);
+  }();
+  CUcontext c = nullptr;
+  if (fn != nullptr && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return c;
+}
+
+// Device address of g_router_scratch on the current device.  Looked up with that
+// device current, on the first call there, and again whenever the thread's current
+// context is no longer the one the address was taken in (a context created anew,
+// e.g. after cudaDeviceReset, loads the module again and may place the array
+// elsewhere).  In host code the symbol itself is only a host-side stand-in, never a
+// device address.
 int router_scratch_address(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return fail(B200MOE_ENODEVICE, "no usable current CUDA device");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  if (g_scratch_ptr[dev] == nullptr || current_context() != g_scratch_ctx[dev]) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(B200MOE_ECUDA, "cudaGetSymbolAddress(router scratch) on device %d: %s", dev,
                   cudaGetErrorString(e));
     g_scratch_ptr[dev] = p;
+    g_scratch_ctx[dev] = current_context();  // the lookup made the primary context current
   }
   *out = g_scratch_ptr[dev];
   return B200MOE_OK;
@@ -1099,9 +1128,10 @@ extern "C" int b200moe_router_noalloc(const void* x, int64_t ldx, int x_dtype, c
                 "b200moe_router_noalloc: T=%d, %d router columns and %d slots need %zu bytes of scratch; "
                 "the built-in scratch holds %zu bytes (use b200moe_router with a caller workspace)",
                 T, E1, num_slots, need, kNoAllocScratchBytes);
-  void* ws = nullptr;
-  int rc = router_scratch_address(&ws);
+  int rc = device_ok();  // a clear error on a device without an sm_100a image, before any lookup
   if (rc) return rc;
+  void* ws = nullptr;
+  if ((rc = router_scratch_address(&ws))) return rc;
   // The completion counter must read zero when the kernels start; a call that was cut
   // short could have left it set, so clear it on the caller's stream every time.
   const cudaError_t e = cudaMemsetAsync(ws, 0, kCounterBytes, static_cast<cudaStream_t>(stream));

@@ -17,6 +17,11 @@ inline int dtype_bytes(int dt) { return dt == kDtypeBF16 ? 2 : 4; }
 // Multiprocessor count of the current device (cached per device).
 int num_sms();
 
+// Upper bound on a persistent grouped-GEMM grid: the SM count, or fewer CTAs when
+// B200MOE_GEMM_MAX_CTAS is set (a test knob: a small grid makes every CTA walk many
+// tiles, the regime of prefill-sized launches, on inputs the checker handles quickly).
+int gemm_grid_limit();
+
 // Programmatic dependent launch on/off (B200MOE_PDL=0 turns it off).
 bool pdl_enabled();
 

@@ -364,7 +364,8 @@ static int run_gemm(const GemmLaunch& L, cudaStream_t stream) {
   }
   const int nt = (L.p.N + S::OUT_COLS - 1) / S::OUT_COLS;
   const int64_t bound = ((L.rows_cap + BMA - 1) / BMA + L.p.P) * static_cast<int64_t>(nt);
-  const int grid = static_cast<int>(bound < num_sms() ? bound : num_sms());
+  const int limit = gemm_grid_limit();
+  const int grid = static_cast<int>(bound < limit ? bound : limit);
   if (grid <= 0) return 0;
   launch_kernel(grouped_gemm_kernel<BN, STAGES, SWIGLU, BMA>, dim3(grid), dim3(GM_THREADS), smem, stream, ma, mb,
                 L.p);

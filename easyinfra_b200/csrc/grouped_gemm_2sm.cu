@@ -417,7 +417,8 @@ static int run_pair(const GemmLaunch& L0, cudaStream_t stream) {
   const int nt = (L.p.N + S::OUT_COLS - 1) / S::OUT_COLS;
   const int groups = L.p.seg_mode ? L.p.seg.G * L.p.P : L.p.P;
   const int64_t bound = ((L.rows_cap + 2 * G2_ROWS - 1) / (2 * G2_ROWS) + groups) * static_cast<int64_t>(nt);
-  const int pairs = static_cast<int>(bound < num_sms() / 2 ? bound : num_sms() / 2);
+  const int limit = gemm_grid_limit() / 2;
+  const int pairs = static_cast<int>(bound < limit ? bound : limit);
   if (pairs <= 0) return 0;
   launch_kernel(grouped_gemm_pair_kernel<STAGES, SWIGLU>, dim3(2 * pairs), dim3(G2_THREADS), S::SMEM_BYTES,
                 stream, ma, mb, L.p);

@@ -328,7 +328,8 @@ static int run_wm(const GemmLaunch& L, cudaStream_t stream) {
   }
   const int nt = (L.p.N + S::FEAT - 1) / S::FEAT;
   const int64_t bound = ((L.rows_cap + NTOK - 1) / NTOK + L.p.P) * static_cast<int64_t>(nt);
-  const int grid = static_cast<int>(bound < num_sms() ? bound : num_sms());
+  const int limit = gemm_grid_limit();
+  const int grid = static_cast<int>(bound < limit ? bound : limit);
   if (grid <= 0) return 0;
   launch_kernel(grouped_gemm_wm_kernel<NTOK, STAGES, SWIGLU, WIDE>, dim3(grid), dim3(WM_THREADS), smem, stream,
                 mw, mx, mx2, L.p);

@@ -159,7 +159,9 @@ B200MOE_API int b200moe_router_sigmoid_grouped(const void* x, int64_t ldx, int x
  * logits), held by every GPU that loads the library until the process exits; calls
  * needing more (see b200moe_router_workspace_bytes) return B200MOE_EUNSUPPORTED.
  * The first call on a device looks the array's address up (cudaGetSymbolAddress), so
- * make that first call before any stream capture.  All calls share the array and it
+ * make that first call before any stream capture; the lookup is repeated when the
+ * calling thread's current context changes (after cudaDeviceReset, for example), so
+ * the first call after such a change must also come before any capture.  All calls share the array and it
  * keeps the last call's contents (each call clears the counter it needs zeroed first):
  * calls that overlap on the GPU race, so serialise them (one stream, or events).
  * It is not usable with b200moe_permute, which needs the workspace of its router call.
