@@ -383,6 +383,26 @@ def run_ours(args):
             del graph, run
         if args.breakdown and with_roofline:
             res["breakdown_us_per_layer"] = op_breakdown(stack, T, x, use_graph, barrier, len(layers))
+        if with_roofline and phase_w == "decode" and layer_rows[0] is not None:
+            # whole layer against HBM: the algorithmic bytes of every stage (prologue,
+            # router, permute, expert GEMMs of the hit slots, shared expert, combine)
+            H, I, K, b = shape.hidden, shape.intermediate, shape.top_k, 2
+            E1 = layers[0].p.gate_w.shape[0]
+            Is = shape.shared_intermediate
+            per = []
+            for r, h in zip(layer_rows, layer_hit):
+                byts = (4 * T * H * b                                   # residual add + RMSNorm
+                        + T * H * b + E1 * H * b + T * K * 8            # router
+                        + T * H * b + r * H * b                         # permute
+                        + h * 3 * H * I * b + 2 * r * H * b + 2 * r * I * b   # SwiGLU + down GEMMs
+                        + (3 * H * Is * b + 2 * T * H * b + 2 * T * Is * b if Is else 0)  # shared expert
+                        + r * H * b + T * H * b)                        # combine
+                per.append(byts)
+            layer_s = ms / 1e3 / len(layers)
+            ach = statistics.mean(per) / layer_s / 1e9
+            res["layer_roofline"] = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                                     "frac": ach / hbm, "bytes_per_layer": statistics.mean(per),
+                                     "us_per_layer": layer_s * 1e6, "peak_kind": f"{peak_kind} HBM copy"}
         if with_roofline and kernel_ms and layer_rows[0] is not None:
             # algorithmic work of the SwiGLU GEMM per launch, averaged over layers
             H, I = shape.hidden, shape.intermediate
@@ -432,6 +452,7 @@ def run_ours(args):
                               if k in r}
                              | {"config": config_dict(shape, wl, len(layers), world, args.transport)}
                              | ({"roofline": r["roofline"]} if "roofline" in r else {})
+                             | ({"layer_roofline": r["layer_roofline"]} if "layer_roofline" in r else {})
                              | ({"clocks": r["clocks"]} if r.get("clocks") else {}))
         if xg is not None:
             exchange_status = max(exchange_status, int(max_over_ranks(float(xg_status.item()))))

@@ -1,9 +1,9 @@
 """Generate the golden fixtures of the MoE hot path by running EasyInfra itself.
 
-Run in a container that has the reference checkout (read-only) at $EASYINFRA_REF
-(default /root/reference):
+Run in a container that has the reference checkout (read-only); its path is given
+by the EASYINFRA_REF environment variable (required):
 
-    python tests/golden/make_golden.py
+    EASYINFRA_REF=<path to the EasyInfra checkout> python tests/golden/make_golden.py
 
 It imports the reference's own code on CPU with import shims (the reference targets
 Python 3.14 / torch 2.13 / transformers 4.57; these only make its modules importable
@@ -47,7 +47,7 @@ import torch.distributed as dist
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
-REF = os.environ.get("EASYINFRA_REF", "/root/reference")
+REF = os.environ.get("EASYINFRA_REF", "")
 
 from easyinfra_b200 import configs as C  # noqa: E402
 from tests.golden import cases  # noqa: E402
@@ -84,6 +84,8 @@ def _import_with_placeholders(modname: str, names):
 
 
 def import_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "easyinfra")):
+        raise SystemExit("set EASYINFRA_REF to the EasyInfra checkout (the directory holding easyinfra/)")
     if not hasattr(dist, "all_gather_single"):
         dist.all_gather_single = dist.all_gather_into_tensor
     for n in ("GroupCommunicator", "ChunkBlock", "RequestHub", "Cache"):
