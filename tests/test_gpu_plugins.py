@@ -13,7 +13,7 @@ from easyinfra_b200 import configs as C
 from easyinfra_b200.block import B200MoeAll2AllBlock
 from easyinfra_b200.experts import B200MoE, register_torch_ops
 from oracle import moe_oracle as O
-from tests.chunk_protocol import ChunkDriver
+from tests.chunk_protocol import load_trace, run_layers
 
 pytestmark = pytest.mark.gpu
 TIGHT_TOL = 6e-3
@@ -87,46 +87,51 @@ def test_block_stages_ep1_match_oracle(cuda_device):
     assert max_rel(res_out, exp_res) < TIGHT_TOL
 
 
-def test_block_two_streams_two_chunks_match_oracle(cuda_device):
-    """The block under ChunkBlock's two-stream protocol with two chunks interleaved stage
-    by stage (compute of both, then communicate of both): each chunk's residual and
-    output equal the oracle's.  At EP size 1 no stage has communication, so nothing
-    orders the comm stream after compute; the block keeps every device read on the
-    compute stream."""
+def _qwen3_blocks(device, ep_group, n_layers, rank=0):
+    """One small Qwen3-shaped B200 block per MoE layer (layer l has layer l's weights;
+    rank `rank` holds its share of the slots)."""
     shape = C.small(C.CONFIGS["qwen3"], hidden=256, intermediate=128)
     E, H, I = shape.num_experts, shape.hidden, shape.intermediate
     g1 = NS(group_size=1, local_rank=0)
-    blk = B200MoeAll2AllBlock(0, H, I, "silu", False, False, E, shape.top_k, shape.norm_topk_prob, False,
-                              None, g1, g1, False, device=cuda_device)
-    gw = C.router_weight(shape, 0)
-    wgu, wd = C.expert_weights(shape, 0, list(range(E)))
-    with torch.no_grad():
-        blk.gate.weight.copy_(gw)
-        blk.experts.experts_gate_up_weight.copy_(wgu)
-        blk.experts.experts_down_weight.copy_(wd)
-    compute_stream, comm_stream = torch.cuda.Stream(cuda_device), torch.cuda.Stream(cuda_device)
-    inputs, drivers = [], []
-    for cid, T in enumerate((48, 5)):
-        res = C.hidden_states(shape, T, seed_offset=10 + cid)
-        hid = C.hidden_states(shape, T, seed_offset=20 + cid)
-        inputs.append((res, hid))
-        drivers.append(ChunkDriver(blk, cid, res.to(cuda_device), hid.to(cuda_device), compute_stream,
-                                    comm_stream))
-    torch.cuda.synchronize()
-    for _ in range(len(blk.stages)):
-        for d in drivers:
-            d.run_compute()
-        for d in drivers:
-            d.run_communicate()
-    torch.cuda.synchronize()
-    for (res, hid), d in zip(inputs, drivers):
-        res_out, hid_out = d.chunk.active_variables
-        r, normed = O.add_rmsnorm(res, hid, torch.ones(H, dtype=res.dtype), 1e-6)
-        tr = O.moe_layer_ep([normed], O.LayerWeights(gw, wgu, wd), shape.top_k, shape.norm_topk_prob,
-                            torch.arange(E).view(1, E), use_eplb=False, fp32_accumulate=True)[0]
-        assert d.chunk.send_token_split == [res.shape[0] * shape.top_k]
-        assert torch.equal(res_out.cpu(), r)
-        assert max_rel(hid_out, tr.out_f32) < TIGHT_TOL
+    blocks, weights = [], []
+    for layer in range(n_layers):
+        blk = B200MoeAll2AllBlock(layer, H, I, "silu", False, False, E, shape.top_k, shape.norm_topk_prob,
+                                  False, None, ep_group, g1, False, device=device)
+        P = blk.num_physical_experts
+        gw = C.router_weight(shape, layer)
+        wgu, wd = C.expert_weights(shape, layer, list(range(E)))
+        with torch.no_grad():
+            blk.gate.weight.copy_(gw)
+            blk.experts.experts_gate_up_weight.copy_(wgu[rank * P:(rank + 1) * P])
+            blk.experts.experts_down_weight.copy_(wd[rank * P:(rank + 1) * P])
+        blocks.append(blk)
+        weights.append(O.LayerWeights(gw, wgu, wd))
+    return shape, blocks, weights
+
+
+@pytest.mark.parametrize("scenario", ["direct_ep1", "pools_ep1"])
+def test_block_under_recorded_chunkblock_protocol(cuda_device, scenario):
+    """Two MoE layers (one block each) and two chunks driven by the stage calls, waits
+    and records that EasyInfra's own ChunkBlock made (tests/golden/chunk_trace.json,
+    recorded from easyinfra/schedule/chunk.py:204-330 with the scheduler's call
+    patterns), on a compute and a comm stream: every layer of every chunk equals the
+    oracle on that layer's actual inputs.  At EP size 1 no stage communicates, so no
+    event orders the comm stream; the block keeps every device read on the compute
+    stream."""
+    shape, blocks, weights = _qwen3_blocks(cuda_device, NS(group_size=1, local_rank=0), 2)
+    E, H = shape.num_experts, shape.hidden
+    trace = load_trace(scenario)
+    inputs = [(C.hidden_states(shape, T, seed_offset=10 + c), C.hidden_states(shape, T, seed_offset=20 + c))
+              for c, T in enumerate((48, 5))]
+    seen = run_layers(trace, blocks, inputs, cuda_device)
+    for c, layers in enumerate(seen):
+        for l, (res_in, hid_in, res_out, hid_out) in enumerate(layers):
+            r, normed = O.add_rmsnorm(res_in, hid_in, torch.ones(H, dtype=res_in.dtype), 1e-6)
+            tr = O.moe_layer_ep([normed], weights[l], shape.top_k, shape.norm_topk_prob,
+                                torch.arange(E).view(1, E), use_eplb=False, fp32_accumulate=True)[0]
+            assert torch.equal(res_out, r), (scenario, c, l)
+            assert max_rel(hid_out, tr.out_f32) < TIGHT_TOL, (scenario, c, l)
+        assert torch.equal(seen[c][1][0], seen[c][0][2])   # layer 1 starts from layer 0's residual
 
 
 def test_cutlass_grouped_gemm_single_op(cuda_device):
