@@ -15,7 +15,9 @@
 //                       fp32 on a cp.async ring; logits rounded to bf16 exactly like
 //                       F.linear's bf16 output.
 //   router_logits_gemv  T <= 256: one CTA per (8 tokens, router column), fixed-order
-//                       reduction.
+//                       reduction; router_logits_gemv_cols, the same reduction for a
+//                       group of columns per CTA with the token rows in registers, once
+//                       there are enough token groups to fill the SMs.
 //   router_logits_f32   SIMT fp32 dot products (fp32 activations).
 //   router_select       one warp per token: fp32 softmax, top-k with ties broken to
 //                       the lowest expert index (warp reductions), renorm, scaling,
@@ -199,6 +201,89 @@ __global__ void __launch_bounds__(256) router_logits_gemv(RouterLogitsParams p) 
     if (p.bias) v += p.bias[e];
     if (sizeof(E) == 2 && p.round_bf16) v = bf16_round(v);
     p.logits[static_cast<int64_t>(t0 + threadIdx.x) * p.E1 + e] = v;
+  }
+}
+
+// Decode batches of 9-256 tokens: one CTA per (RG tokens, CG router columns).  The
+// CTA's token rows are held in registers (NX 16-byte vectors per token and thread,
+// H == NX * 256 * V) and reused for its CG columns, so x is read from L2 once per
+// column group instead of once per column.  Every column is reduced exactly like
+// router_logits_gemv (same per-thread order, same shuffle tree, same fixed cross-warp
+// order): the logits are bit-identical to that kernel's for every CG.
+template <typename E, int NX, int CG>
+__global__ void __launch_bounds__(256) router_logits_gemv_cols(RouterLogitsParams p) {
+  __shared__ float red[CG][8][RG];
+  pdl_trigger();
+  const int col0 = blockIdx.y * CG;
+  const int ncols = min(CG, p.E1 - col0);
+  if (blockIdx.x == 0)  // this CTA's router rows toward L2 before the wait (once per column group)
+    prefetch_l2_lines(static_cast<const E*>(p.w) + static_cast<int64_t>(col0) * p.H,
+                      static_cast<int64_t>(ncols) * p.H * sizeof(E));
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * RG;
+  const int nt = min(RG, p.T - t0);
+  constexpr int V = 16 / sizeof(E);
+  const E* x = static_cast<const E*>(p.x) + static_cast<int64_t>(t0) * p.ldx;
+  uint4 xv[NX][RG];
+#pragma unroll
+  for (int j = 0; j < NX; ++j) {
+    const int c = (threadIdx.x + j * 256) * V;
+#pragma unroll
+    for (int i = 0; i < RG; ++i)
+      xv[j][i] = (i < nt) ? __ldg(reinterpret_cast<const uint4*>(x + i * p.ldx + c)) : make_uint4(0, 0, 0, 0);
+  }
+  const E* wbase = static_cast<const E*>(p.w) + static_cast<int64_t>(col0) * p.H;
+  uint4 wv[NX];
+#pragma unroll
+  for (int j = 0; j < NX; ++j) wv[j] = __ldg(reinterpret_cast<const uint4*>(wbase + (threadIdx.x + j * 256) * V));
+#pragma unroll 1
+  for (int cc = 0; cc < ncols; ++cc) {
+    uint4 wn[NX];  // next column's weights, loaded before this column's arithmetic
+    if (cc + 1 < ncols) {
+#pragma unroll
+      for (int j = 0; j < NX; ++j)
+        wn[j] = __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<int64_t>(cc + 1) * p.H +
+                                                     (threadIdx.x + j * 256) * V));
+    }
+    float acc[RG];
+#pragma unroll
+    for (int i = 0; i < RG; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < NX; ++j) {
+      const E* we = reinterpret_cast<const E*>(&wv[j]);
+#pragma unroll
+      for (int i = 0; i < RG; ++i) {
+        const E* xe = reinterpret_cast<const E*>(&xv[j][i]);
+#pragma unroll
+        for (int q = 0; q < V; ++q) acc[i] = fmaf(static_cast<float>(xe[q]), static_cast<float>(we[q]), acc[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < RG; ++i) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < RG; ++i) red[cc][warp][i] = acc[i];
+    }
+    if (cc + 1 < ncols) {
+#pragma unroll
+      for (int j = 0; j < NX; ++j) wv[j] = wn[j];
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < ncols * RG; idx += blockDim.x) {
+    const int cc = idx / RG, i = idx - cc * RG;
+    if (i >= nt) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v += red[cc][q][i];
+    const int e = col0 + cc;
+    if (p.bias) v += p.bias[e];
+    if (sizeof(E) == 2 && p.round_bf16) v = bf16_round(v);
+    p.logits[static_cast<int64_t>(t0 + i) * p.E1 + e] = v;
   }
 }
 
@@ -741,6 +826,33 @@ int launch_router_small_fused(const RouterLogitsParams& lp, const RouterSelectPa
 }
 
 // ------------------------------------------------------------------ host launchers
+// Router columns per CTA of the GEMV (1: router_logits_gemv).  Column groups need the
+// token rows to fit in registers (H == NX * 256 * V, NX <= 2); the widest group that
+// still gives every SM a CTA is taken.  B200MOE_ROUTER_COLS=c forces c
+// (1, 2, 4, 8 or 16) for tuning.
+static int router_gemv_cols(int groups, int E1, int H, int x_dtype) {
+  const int V = 16 / dtype_bytes(x_dtype);
+  const int nx = H / (256 * V);
+  if (nx < 1 || nx > 2 || nx * 256 * V != H) return 1;
+  const char* env = getenv("B200MOE_ROUTER_COLS");
+  if (env != nullptr) {
+    const int c = atoi(env);
+    return (c == 2 || c == 4 || c == 8 || c == 16) ? c : 1;
+  }
+  int cg = 1;
+  while (cg < 16 && static_cast<int64_t>(groups) * ((E1 + 2 * cg - 1) / (2 * cg)) >= num_sms()) cg *= 2;
+  return cg;
+}
+
+template <typename E>
+static void launch_gemv_cols(dim3 grid, int cg, int nx, const RouterLogitsParams& p, cudaStream_t stream) {
+#define B200MOE_GEMV_COLS(NXV, CGV) \
+  if (nx == NXV && cg == CGV) { launch_kernel(router_logits_gemv_cols<E, NXV, CGV>, grid, dim3(256), 0, stream, p); return; }
+  B200MOE_GEMV_COLS(1, 2) B200MOE_GEMV_COLS(1, 4) B200MOE_GEMV_COLS(1, 8) B200MOE_GEMV_COLS(1, 16)
+  B200MOE_GEMV_COLS(2, 2) B200MOE_GEMV_COLS(2, 4) B200MOE_GEMV_COLS(2, 8) B200MOE_GEMV_COLS(2, 16)
+#undef B200MOE_GEMV_COLS
+}
+
 int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t stream) {
   if (p.T == 0) return 0;
   // GEMV (one CTA per (8-token group, column)) up to this many tokens, tensor-core
@@ -750,7 +862,18 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
     return v ? atoi(v) : 256;
   }();
   if (p.T <= gemv_max) {
-    const dim3 grid((p.T + RG - 1) / RG, p.E1);
+    const int groups = (p.T + RG - 1) / RG;
+    const int cg = router_gemv_cols(groups, p.E1, p.H, x_dtype);
+    if (cg > 1) {
+      const dim3 grid(groups, (p.E1 + cg - 1) / cg);
+      const int nx = p.H / (256 * (16 / dtype_bytes(x_dtype)));
+      if (x_dtype == kDtypeBF16)
+        launch_gemv_cols<__nv_bfloat16>(grid, cg, nx, p, stream);
+      else
+        launch_gemv_cols<float>(grid, cg, nx, p, stream);
+      return 0;
+    }
+    const dim3 grid(groups, p.E1);
     if (x_dtype == kDtypeBF16)
       launch_kernel(router_logits_gemv<__nv_bfloat16>, grid, dim3(256), 0, stream, p);
     else

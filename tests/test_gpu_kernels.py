@@ -331,6 +331,28 @@ def test_router_logits_paths_match_cpu_linear(cuda_device, T, E1, H, bias):
     assert float(((got - ref).abs() > 0).float().mean()) < 0.05
 
 
+@pytest.mark.parametrize("T,E1,H,dtype,bias", [(256, 128, 2048, torch.bfloat16, True),
+                                               (131, 61, 2048, torch.bfloat16, False),
+                                               (64, 8, 4096, torch.bfloat16, True),
+                                               (200, 37, 1024, torch.float32, True)])
+def test_router_gemv_column_groups_bit_identical(cuda_device, monkeypatch, T, E1, H, dtype, bias):
+    """The decode-batch logits GEMV with 2..16 router columns per CTA (token rows held
+    in registers) reduces every column exactly like the one-column kernel: the logits
+    are bit-identical for every group width, including partial groups and a partial
+    last token group."""
+    g = torch.Generator().manual_seed(T * 3 + E1)
+    x = torch.randn(T, H, generator=g).to(dtype).to(cuda_device)
+    w = (torch.randn(E1, H, generator=g) * 0.02).to(dtype).to(cuda_device)
+    b = torch.randn(E1, generator=g).to(cuda_device) if bias else None
+    outs = {}
+    for cols in ("1", "2", "4", "8", "16"):
+        monkeypatch.setenv("B200MOE_ROUTER_COLS", cols)
+        outs[cols] = ops.router(x, w, 2, renorm=True, gate_bias=b, num_slots=E1, keep_logits=True).logits
+    torch.cuda.synchronize()
+    for cols, lg in outs.items():
+        assert torch.equal(lg, outs["1"]), cols
+
+
 @pytest.mark.parametrize("name", ["dsv3_moonlight", "dsv3_v3"])
 def test_router_sigmoid_grouped_matches_reference(cuda_device, name):
     """DeepSeek-V3 router: fp32 logits close to the reference gate's; selection
