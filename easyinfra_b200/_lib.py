@@ -42,6 +42,13 @@ SIGNATURES = {
          c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p, c_size_t, c_void_p, c_void_p],
     ),
+    "b200moe_add_rmsnorm_router_permute": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_float, c_int64, c_void_p, c_void_p, c_int64, c_int,
+         c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p,
+         c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p],
+    ),
     "b200moe_router_sigmoid_grouped": (
         c_int,
         [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,

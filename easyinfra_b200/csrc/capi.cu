@@ -174,7 +174,7 @@ int select_common(const float* logits, int has_shared_gate, int T, int E, int K,
                   const RouterWs& ws, int* status, cudaStream_t stream, int scoring = 0,
                   int n_group = 1, int topk_group = 1, const float* correction_bias = nullptr,
                   const RouterLogitsParams* fuse_lp = nullptr, const AddNormParams* fuse_np = nullptr,
-                  int x_dtype = 0) {
+                  int x_dtype = 0, const SmallPermuteOut* fuse_po = nullptr) {
   RouterSelectParams s;
   s.scoring = scoring;
   s.n_group = n_group;
@@ -207,7 +207,7 @@ int select_common(const float* logits, int has_shared_gate, int T, int E, int K,
   s.status = status;
   if (fuse_lp != nullptr) {
     // logits (and the prologue) fused with the selection: one launch for small batches
-    if (launch_router_small_fused(*fuse_lp, s, fuse_np, x_dtype, stream))
+    if (launch_router_small_fused(*fuse_lp, s, fuse_np, x_dtype, stream, fuse_po))
       return fail(B200MOE_ECUDA, "router_small_fused: %s", cudaGetErrorString(cudaGetLastError()));
     return check_launch("router_small_fused");
   }
@@ -304,13 +304,21 @@ int b200moe_router(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
                        status, st, 0, 1, 1, nullptr, fuse ? &lp : nullptr, nullptr, x_dtype);
 }
 
-int b200moe_add_rmsnorm_router(const void* residual, const void* hidden, const void* norm_weight, float eps,
-                               int64_t ld, void* residual_out, void* normed, int64_t ld_normed, int x_dtype,
-                               const void* gate_w, const float* gate_bias, int has_shared_gate, int T, int H, int E,
-                               int K, int renorm, float scale, const int32_t* log2phy, const int32_t* rep_count,
-                               int max_rep, int num_slots, int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
-                               float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets, float* logits_out,
-                               void* workspace, size_t workspace_bytes, int* status, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// b200moe_add_rmsnorm_router, and with `send` / `pos_of` also the permute of the routed
+// rows (b200moe_add_rmsnorm_router_permute): fused into the one launch for T <= 8,
+// otherwise b200moe_permute after the router.
+int add_rmsnorm_router_impl(const void* residual, const void* hidden, const void* norm_weight, float eps,
+                            int64_t ld, void* residual_out, void* normed, int64_t ld_normed, int x_dtype,
+                            const void* gate_w, const float* gate_bias, int has_shared_gate, int T, int H, int E,
+                            int K, int renorm, float scale, const int32_t* log2phy, const int32_t* rep_count,
+                            int max_rep, int num_slots, int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                            float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets, float* logits_out,
+                            void* workspace, size_t workspace_bytes, int* status, void* stream, void* send,
+                            int32_t* pos_of) {
   int rc;
   if ((rc = device_ok())) return rc;
   if (x_dtype != B200MOE_DTYPE_BF16 && x_dtype != B200MOE_DTYPE_F32)
@@ -322,15 +330,22 @@ int b200moe_add_rmsnorm_router(const void* residual, const void* hidden, const v
                 (hidden && !aligned16(hidden)) || !aligned16(norm_weight) || (ld * eb) % 16 != 0 ||
                 (ld_normed * eb) % 16 != 0 || ld < H || ld_normed < H))
     return fail(B200MOE_EINVAL, "prologue rows must be 16-byte aligned with 16-byte strides");
+  const bool with_permute = send != nullptr || pos_of != nullptr;
+  if (with_permute && (!send || !pos_of || !aligned16(send) || (static_cast<int64_t>(H) * eb) % 16 != 0))
+    return fail(B200MOE_EINVAL, "send and pos_of must both be given, send 16-byte aligned with 16-byte rows");
   const bool fuse = router_small_fused_ok(T, H, x_dtype, num_slots, 0, true);
   if (!fuse) {
-    // larger batches: the prologue kernel, then the router on its output
+    // larger batches: the prologue kernel, then the router on its output (then the permute)
     if ((rc = b200moe_add_rmsnorm(residual, hidden, norm_weight, eps, T, H, x_dtype, ld, residual_out, normed,
                                   ld_normed, stream)))
       return rc;
-    return b200moe_router(normed, ld_normed, x_dtype, gate_w, gate_bias, has_shared_gate, T, H, E, K, renorm, scale,
-                          log2phy, rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate,
-                          slot_counts, slot_offsets, logits_out, workspace, workspace_bytes, status, stream);
+    if ((rc = b200moe_router(normed, ld_normed, x_dtype, gate_w, gate_bias, has_shared_gate, T, H, E, K, renorm,
+                             scale, log2phy, rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate,
+                             slot_counts, slot_offsets, logits_out, workspace, workspace_bytes, status, stream)))
+      return rc;
+    if (!with_permute) return B200MOE_OK;
+    return b200moe_permute(normed, ld_normed, x_dtype, T, H, K, E + (has_shared_gate ? 1 : 0), phys_ids, num_slots,
+                           send, pos_of, nullptr, nullptr, workspace, workspace_bytes, stream);
   }
   rc = check_select_args(T, E, K, num_slots, log2phy, rep_count, max_rep, topk_ids, topk_w, phys_ids, slot_counts,
                          slot_offsets, has_shared_gate, shared_gate);
@@ -361,11 +376,49 @@ int b200moe_add_rmsnorm_router(const void* residual, const void* hidden, const v
   lp.H = H;
   lp.E1 = E1;
   lp.logits = logits_out ? logits_out : ws.logits;
+  SmallPermuteOut po;
+  po.send = send;
+  po.pos_of = pos_of;
+  po.row_bytes = H * eb;
   return select_common(lp.logits, has_shared_gate, T, E, K, renorm, scale, x_dtype == B200MOE_DTYPE_BF16, log2phy,
                        rep_count, max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate, slot_counts,
                        slot_offsets, ws, status, static_cast<cudaStream_t>(stream), 0, 1, 1, nullptr, &lp, &np,
-                       x_dtype);
+                       x_dtype, with_permute ? &po : nullptr);
 }
+
+}  // namespace
+
+extern "C" {
+
+int b200moe_add_rmsnorm_router(const void* residual, const void* hidden, const void* norm_weight, float eps,
+                               int64_t ld, void* residual_out, void* normed, int64_t ld_normed, int x_dtype,
+                               const void* gate_w, const float* gate_bias, int has_shared_gate, int T, int H, int E,
+                               int K, int renorm, float scale, const int32_t* log2phy, const int32_t* rep_count,
+                               int max_rep, int num_slots, int32_t* topk_ids, float* topk_w, int32_t* phys_ids,
+                               float* shared_gate, int32_t* slot_counts, int32_t* slot_offsets, float* logits_out,
+                               void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  return add_rmsnorm_router_impl(residual, hidden, norm_weight, eps, ld, residual_out, normed, ld_normed, x_dtype,
+                                 gate_w, gate_bias, has_shared_gate, T, H, E, K, renorm, scale, log2phy, rep_count,
+                                 max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate, slot_counts,
+                                 slot_offsets, logits_out, workspace, workspace_bytes, status, stream, nullptr,
+                                 nullptr);
+}
+
+int b200moe_add_rmsnorm_router_permute(const void* residual, const void* hidden, const void* norm_weight, float eps,
+                                       int64_t ld, void* residual_out, void* normed, int64_t ld_normed, int x_dtype,
+                                       const void* gate_w, const float* gate_bias, int has_shared_gate, int T, int H,
+                                       int E, int K, int renorm, float scale, const int32_t* log2phy,
+                                       const int32_t* rep_count, int max_rep, int num_slots, int32_t* topk_ids,
+                                       float* topk_w, int32_t* phys_ids, float* shared_gate, int32_t* slot_counts,
+                                       int32_t* slot_offsets, float* logits_out, void* send, int32_t* pos_of,
+                                       void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  if (T > 0 && (send == nullptr || pos_of == nullptr)) return fail(B200MOE_EINVAL, "null send / pos_of");
+  return add_rmsnorm_router_impl(residual, hidden, norm_weight, eps, ld, residual_out, normed, ld_normed, x_dtype,
+                                 gate_w, gate_bias, has_shared_gate, T, H, E, K, renorm, scale, log2phy, rep_count,
+                                 max_rep, num_slots, topk_ids, topk_w, phys_ids, shared_gate, slot_counts,
+                                 slot_offsets, logits_out, workspace, workspace_bytes, status, stream, send, pos_of);
+}
+
 
 int b200moe_router_sigmoid_grouped(const void* x, int64_t ldx, int x_dtype, const void* gate_w,
                                    const float* correction_bias, int T, int H, int E, int K,

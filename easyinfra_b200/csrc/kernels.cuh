@@ -345,8 +345,16 @@ int launch_router_logits(const RouterLogitsParams& p, int x_dtype, cudaStream_t 
 // Small batches (T <= 8): logits, selection and optionally the block prologue in one
 // launch (router.cu).  sp must describe one token block (nblocks 1).
 bool router_small_fused_ok(int T, int H, int x_dtype, int num_slots, int scoring, bool has_norm);
+// Optional permute outputs of the fused small-batch router (one token block): the send
+// rows in (physical slot, t*K+k) order and each entry's send row, exactly as
+// permute_rows writes them.
+struct SmallPermuteOut {
+  void* send = nullptr;       // [T*K, H], row stride row_bytes
+  int32_t* pos_of = nullptr;  // [T, K]
+  int row_bytes = 0;
+};
 int launch_router_small_fused(const RouterLogitsParams& lp, const RouterSelectParams& sp, const AddNormParams* np,
-                              int x_dtype, cudaStream_t stream);
+                              int x_dtype, cudaStream_t stream, const SmallPermuteOut* po = nullptr);
 int launch_grouped_gemm_f32(const GemmF32Params& p, bool swiglu, cudaStream_t stream);
 int launch_router_select(const RouterSelectParams& p, cudaStream_t stream);
 int launch_permute(const PermuteParams& p, cudaStream_t stream);

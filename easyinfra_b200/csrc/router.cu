@@ -26,7 +26,9 @@
 //                       slot offsets and per-(slot, block) write offsets for the
 //                       permute kernel.
 //   router_small_fused  T <= 8: optional residual add + RMSNorm, the GEMV logits and
-//                       the selection in one launch, with the bits of the kernels above.
+//                       the selection in one launch, with the bits of the kernels above;
+//                       optionally also the permute (send rows straight from the rows
+//                       the CTA holds in shared memory).
 #include <cstdlib>
 
 #include <atomic>
@@ -701,7 +703,8 @@ constexpr size_t kFusedSmemMax = 160 * 1024;
 template <typename E>
 __global__ void __launch_bounds__(256) router_small_fused(const __grid_constant__ RouterLogitsParams lp,
                                                           const __grid_constant__ RouterSelectParams sp,
-                                                          const __grid_constant__ AddNormParams np, int has_norm) {
+                                                          const __grid_constant__ AddNormParams np, int has_norm,
+                                                          const __grid_constant__ SmallPermuteOut po) {
   extern __shared__ __align__(16) uint8_t dyn[];
   __shared__ float red[8][RG];
   __shared__ float nred[NORM_THREADS / 32];
@@ -785,6 +788,44 @@ __global__ void __launch_bounds__(256) router_small_fused(const __grid_constant_
   select_tokens_any(sp, 0, T, hist);
   __syncthreads();
   select_finish_one_block(sp, hist);
+  if (po.send == nullptr) return;
+
+  // The permute of the one token block (permute_rows' order: within a slot, flat
+  // t*K+k order), with the rows taken from shared memory: hist holds the slot offsets,
+  // phys_ids were written by this CTA above.
+  __shared__ int32_t s_pos[RG * 8];
+  const int ne = T * sp.K;
+  __syncthreads();
+  if (warp == 0) {
+    for (int base = 0; base < ne; base += 32) {
+      const int i = base + lane;
+      const bool valid = i < ne;
+      const int s = valid ? sp.phys_ids[i] : -1 - lane;
+      const uint32_t peers = __match_any_sync(0xffffffffu, s);
+      const int leader = __ffs(peers) - 1;
+      int start = 0;
+      if (valid && lane == leader) {
+        start = hist[s];
+        hist[s] = start + __popc(peers);
+      }
+      start = __shfl_sync(0xffffffffu, start, leader);
+      if (valid) {
+        const int d = start + __popc(peers & ((1u << lane) - 1u));
+        s_pos[i] = d;
+        po.pos_of[i] = d;
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  const int vpr = H / V;
+  for (int idx = threadIdx.x; idx < ne * vpr; idx += blockDim.x) {
+    const int i = idx / vpr, v = idx - i * vpr;
+    const int t = i / sp.K;
+    *reinterpret_cast<uint4*>(static_cast<uint8_t*>(po.send) + static_cast<int64_t>(s_pos[i]) * po.row_bytes +
+                              static_cast<int64_t>(v) * 16) =
+        *reinterpret_cast<const uint4*>(xs + static_cast<int64_t>(t) * H + static_cast<int64_t>(v) * V);
+  }
 }
 
 size_t router_small_fused_smem(int T, int H, int x_dtype, int num_slots, int scoring) {
@@ -800,7 +841,7 @@ bool router_small_fused_ok(int T, int H, int x_dtype, int num_slots, int scoring
 }
 
 int launch_router_small_fused(const RouterLogitsParams& lp, const RouterSelectParams& sp, const AddNormParams* np,
-                              int x_dtype, cudaStream_t stream) {
+                              int x_dtype, cudaStream_t stream, const SmallPermuteOut* po) {
   static std::atomic<uint64_t> attr_set_mask{0};  // one bit per device ordinal
   int dev = 0;
   cudaGetDevice(&dev);
@@ -814,14 +855,15 @@ int launch_router_small_fused(const RouterLogitsParams& lp, const RouterSelectPa
     attr_set_mask.fetch_or(bit, std::memory_order_release);
   }
   AddNormParams none{};
+  const SmallPermuteOut no_perm{};
   const size_t smem = router_small_fused_smem(lp.T, lp.H, x_dtype, sp.num_slots, sp.scoring);
   cudaError_t e;
   if (x_dtype == kDtypeBF16)
     e = launch_kernel(router_small_fused<__nv_bfloat16>, dim3(lp.E1), dim3(256), smem, stream, lp, sp,
-                      np ? *np : none, np ? 1 : 0);
+                      np ? *np : none, np ? 1 : 0, po ? *po : no_perm);
   else
     e = launch_kernel(router_small_fused<float>, dim3(lp.E1), dim3(256), smem, stream, lp, sp, np ? *np : none,
-                      np ? 1 : 0);
+                      np ? 1 : 0, po ? *po : no_perm);
   return e == cudaSuccess ? 0 : -2;
 }
 

@@ -158,10 +158,13 @@ class MoELayer:
                            num_slots=self.G * self.P, workspace=self.ws, status=self.status)
         return r
 
-    def route_and_permute(self, x: torch.Tensor, pre: Optional[ops.RouterOutput] = None) -> DispatchState:
-        """Router + permute into a local send buffer (no exchange)."""
+    def route_and_permute(self, x: torch.Tensor, pre: Optional[ops.RouterOutput] = None,
+                          pre_perm: Optional[ops.PermuteOutput] = None) -> DispatchState:
+        """Router + permute into a local send buffer (no exchange); pre / pre_perm: this
+        batch's routing and permutation when the caller already ran them."""
         r = self.route(x, pre)
-        perm = ops.permute(x, r, num_slots=self.G * self.P, E1=self.p.gate_w.shape[0])
+        perm = pre_perm if pre_perm is not None else ops.permute(x, r, num_slots=self.G * self.P,
+                                                                 E1=self.p.gate_w.shape[0])
         return DispatchState(T=x.shape[0], route=r, perm=perm)
 
     def exchange_counts(self, st: DispatchState) -> np.ndarray:
@@ -240,15 +243,21 @@ class MoELayer:
         if nbuf is None:
             nbuf = self._normed[key] = torch.empty_like(residual)
         if self.scoring == "softmax" and residual.shape[0] <= 8:
-            # decode-sized batch: prologue, logits and selection in one launch
+            # decode-sized batch: prologue, logits and selection in one launch; on one
+            # rank the permute joins it (the send rows come from the launch's own copy
+            # of the normed rows)
             l2p = self.log2phy if self.use_map else None
             rep = self.rep_count if self.use_map else None
-            ro, normed, r = ops.add_rmsnorm_router(
+            local = self.G == 1 and self.exchange is None and residual.shape[1] == residual.stride(0)
+            res = ops.add_rmsnorm_router(
                 residual, hidden, self.p.norm_weight, self.p.norm_eps, self.p.gate_w, self.top_k,
                 renorm=self.norm_topk_prob, residual_out=residual_out, normed=nbuf,
                 gate_bias=self.p.gate_bias, scale=self.scale, has_shared_gate=self.shared_gate,
                 log2phy=l2p, rep_count=rep, num_slots=self.G * self.P, workspace=self.ws,
-                status=self.status)
+                status=self.status, permute=local)
+            ro, normed, r = res[:3]
+            if local:
+                return ro, self._forward_local(normed, out, r, res[3])
             return ro, self.forward(normed, out=out, pre=r)
         ro, normed = ops.add_rmsnorm(residual, hidden, self.p.norm_weight, self.p.norm_eps,
                                      residual_out=residual_out, normed=nbuf)
@@ -263,9 +272,10 @@ class MoELayer:
                 and T * self.top_k <= 48 * self.P)
 
     def _forward_local(self, x: torch.Tensor, out: Optional[torch.Tensor],
-                       pre: Optional[ops.RouterOutput] = None) -> torch.Tensor:
+                       pre: Optional[ops.RouterOutput] = None,
+                       pre_perm: Optional[ops.PermuteOutput] = None) -> torch.Tensor:
         if not self._overlap(x.shape[0]):
-            st = self.route_and_permute(x, pre)
+            st = self.route_and_permute(x, pre, pre_perm)
             self.shared_expert(x, st)
             return self.unpermute(st, self.experts_local(st), out)
         cur = torch.cuda.current_stream(self.device)
@@ -276,7 +286,7 @@ class MoELayer:
         held = DispatchState(T=x.shape[0], route=None, perm=None)
         with torch.cuda.stream(side):
             self.shared_expert(x, held)
-        st = self.route_and_permute(x, pre)
+        st = self.route_and_permute(x, pre, pre_perm)
         y = self.experts_local(st)
         cur.wait_stream(side)                       # join before the combine reads it
         held.shared_out.record_stream(cur)

@@ -173,10 +173,14 @@ def add_rmsnorm_router(residual: torch.Tensor, hidden: Optional[torch.Tensor], n
                        gate_bias: Optional[torch.Tensor] = None, scale: float = 1.0,
                        has_shared_gate: bool = False, log2phy: Optional[torch.Tensor] = None,
                        rep_count: Optional[torch.Tensor] = None, num_slots: Optional[int] = None,
-                       workspace: Optional[Workspace] = None, status: Optional[torch.Tensor] = None):
+                       workspace: Optional[Workspace] = None, status: Optional[torch.Tensor] = None,
+                       permute: bool = False, send: Optional[torch.Tensor] = None):
     """The block prologue (residual += hidden; normed = RMSNorm) and the router in one
     call: one launch for batches of up to 8 tokens.  Returns (residual_out, normed,
-    RouterOutput); bit-identical to add_rmsnorm followed by router."""
+    RouterOutput); bit-identical to add_rmsnorm followed by router.  With permute=True
+    the routed rows are permuted too (in the same launch up to 8 tokens; `send` is the
+    optional [>= T*K, H] send buffer) and a PermuteOutput is returned fourth,
+    bit-identical to calling permute afterwards."""
     _need_cuda(residual, hidden, norm_weight, gate_w, gate_bias, log2phy, rep_count, status)
     residual = _rows_contig(residual)
     T, H = residual.shape
@@ -190,12 +194,26 @@ def add_rmsnorm_router(residual: torch.Tensor, hidden: Optional[torch.Tensor], n
         raise ValueError("residual_out must have residual's row stride")
     o = _router_outputs(T, H, residual.dtype, residual.device, gate_w, top_k, gate_bias, has_shared_gate, log2phy,
                         rep_count, num_slots, False, workspace)
-    _lib.call("b200moe_add_rmsnorm_router", residual.data_ptr(), _ptr(hidden),
-              norm_weight.contiguous().data_ptr(), float(eps), residual.stride(0), ro.data_ptr(), nm.data_ptr(),
-              nm.stride(0), _dtype_code(residual),
-              *_router_tail(o, T, H, top_k, renorm, scale, has_shared_gate, status))
-    _count(0 if T == 0 else (1 if T <= 8 else 3))
-    return ro, nm, _router_result(o)
+    head = (residual.data_ptr(), _ptr(hidden), norm_weight.contiguous().data_ptr(), float(eps), residual.stride(0),
+            ro.data_ptr(), nm.data_ptr(), nm.stride(0), _dtype_code(residual))
+    if not permute:
+        _lib.call("b200moe_add_rmsnorm_router", *head, *_router_tail(o, T, H, top_k, renorm, scale,
+                                                                     has_shared_gate, status))
+        _count(0 if T == 0 else (1 if T <= 8 else 3))
+        return ro, nm, _router_result(o)
+    if nm.stride(0) != H:
+        raise ValueError("the permute reads normed rows with row stride H")
+    sb = send if send is not None else torch.empty(T * top_k, H, dtype=residual.dtype, device=residual.device)
+    if sb.shape[0] < T * top_k or sb.shape[1] != H or not sb.is_contiguous():
+        raise ValueError("send buffer must be contiguous [>= T*K, H]")
+    pos_of = torch.empty(T, top_k, dtype=torch.int32, device=residual.device)
+    tail = list(_router_tail(o, T, H, top_k, renorm, scale, has_shared_gate, status))
+    # the router tail ends (..., logits_out, workspace, workspace_bytes, status, stream):
+    # send and pos_of go after logits_out
+    tail[-4:-4] = [sb.data_ptr(), pos_of.data_ptr()]
+    _lib.call("b200moe_add_rmsnorm_router_permute", *head, *tail)
+    _count(0 if T == 0 else (1 if T <= 8 else 4))
+    return ro, nm, _router_result(o), PermuteOutput(sb, pos_of, None, None)
 
 
 def router_sigmoid_grouped(x: torch.Tensor, gate_w: torch.Tensor, correction_bias: torch.Tensor,

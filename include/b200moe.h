@@ -128,6 +128,29 @@ B200MOE_API int b200moe_add_rmsnorm_router(const void* residual, const void* hid
                                            int* status, void* stream);
 
 /*
+ * b200moe_add_rmsnorm_router followed by b200moe_permute on `normed`: additionally
+ * writes send [T*K, H] (rows in (physical slot, t*K+k) order, row stride H elements)
+ * and pos_of [T, K] (the send row of each (t, k)), bit-identical to calling
+ * b200moe_permute after the router (send_token / send_slot are not produced).  For
+ * T <= 8 on one rank it is a single launch: the router's last CTA, which holds the
+ * normed rows in shared memory and every slot offset, ranks the entries and writes the
+ * send rows itself.  Replaces MoeAll2AllBlock.all2all_chunk_routing_compute's
+ * prologue, routing and permutation (easyinfra/generation/blocks/moe/
+ * moe_all2all.py:331-356) at decode batch sizes.
+ */
+B200MOE_API int b200moe_add_rmsnorm_router_permute(const void* residual, const void* hidden,
+                                                   const void* norm_weight, float eps, int64_t ld,
+                                                   void* residual_out, void* normed, int64_t ld_normed,
+                                                   int x_dtype, const void* gate_w, const float* gate_bias,
+                                                   int has_shared_gate, int T, int H, int E, int K, int renorm,
+                                                   float scale, const int32_t* log2phy, const int32_t* rep_count,
+                                                   int max_rep, int num_slots, int32_t* topk_ids, float* topk_w,
+                                                   int32_t* phys_ids, float* shared_gate, int32_t* slot_counts,
+                                                   int32_t* slot_offsets, float* logits_out, void* send,
+                                                   int32_t* pos_of, void* workspace, size_t workspace_bytes,
+                                                   int* status, void* stream);
+
+/*
  * Router of the DeepSeek-V3 family: fp32 logits x·W_gᵀ, sigmoid scores, choice =
  * score + correction_bias, keep the topk_group groups (E / n_group consecutive
  * experts each) with the largest sum of their two best choices, top-K over the

@@ -14,6 +14,7 @@ import torch
 
 from easyinfra_b200 import configs as C
 from easyinfra_b200 import ops
+from easyinfra_b200.placement import Placement
 from oracle import moe_oracle as O
 from tests.conftest import load_golden
 from tests.golden import cases
@@ -437,6 +438,40 @@ def test_fused_prologue_router_equals_separate_calls(cuda_device, T):
     for a, c in [(r.topk_ids, r2.topk_ids), (r.topk_weights, r2.topk_weights), (r.phys_ids, r2.phys_ids),
                  (r.slot_counts, r2.slot_counts), (r.slot_offsets, r2.slot_offsets)]:
         assert torch.equal(a, c)
+
+
+@pytest.mark.parametrize("T", [1, 3, 8, 12])
+@pytest.mark.parametrize("E,H,K,shared,eplb", [(128, 2048, 8, False, True), (60, 1024, 4, True, False),
+                                               (8, 4096, 2, False, False)])
+def test_fused_prologue_router_permute_equals_separate_calls(cuda_device, T, E, H, K, shared, eplb):
+    """add_rmsnorm_router(permute=True) (one launch up to 8 tokens: the router's last
+    CTA writes the send rows from shared memory; above 8 the separate kernels) equals
+    add_rmsnorm, router and permute called one after the other: residual, normed,
+    routing, send rows and send positions bit for bit."""
+    g = torch.Generator().manual_seed(T * 7 + E)
+    d = cuda_device
+    res = torch.randn(T, H, generator=g).to(torch.bfloat16).to(d)
+    hid = torch.randn(T, H, generator=g).to(torch.bfloat16).to(d)
+    nw = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(d)
+    w = (torch.randn(E + int(shared), H, generator=g) * 0.02).to(torch.bfloat16).to(d)
+    l2p = rep = None
+    slots = E
+    if eplb:
+        pl = Placement(C.load_placement(C.CONFIGS["qwen3"].placement, 0, 8), E)
+        l2p, rep = pl.device_tables(d)
+        slots = pl.num_slots
+    kw = dict(renorm=True, has_shared_gate=shared, log2phy=l2p, rep_count=rep, num_slots=slots)
+    ro, nm, r, perm = ops.add_rmsnorm_router(res, hid, nw, 1e-6, w, K, permute=True, **kw)
+    ro2, nm2 = ops.add_rmsnorm(res, hid, nw, 1e-6)
+    r2 = ops.router(nm2, w, K, **kw)
+    perm2 = ops.permute(nm2, r2, num_slots=slots, E1=w.shape[0])
+    torch.cuda.synchronize()
+    assert torch.equal(ro, ro2) and torch.equal(nm, nm2)
+    for a, c in [(r.topk_ids, r2.topk_ids), (r.topk_weights, r2.topk_weights), (r.phys_ids, r2.phys_ids),
+                 (r.slot_counts, r2.slot_counts), (r.slot_offsets, r2.slot_offsets)]:
+        assert torch.equal(a, c)
+    assert torch.equal(perm.pos_of, perm2.pos_of)
+    assert torch.equal(perm.send[:T * K], perm2.send[:T * K])
 
 
 @pytest.mark.parametrize("T", [2, 8])
