@@ -494,6 +494,8 @@ def run_ours(args):
         "clocks": main["clocks"],
         "secondary": secondary,
     }
+    if "layer_roofline" in main:
+        line["layer_roofline"] = main["layer_roofline"]
     if "breakdown_us_per_layer" in main:
         line["breakdown_us_per_layer"] = main["breakdown_us_per_layer"]
     if exchange_status:

@@ -372,13 +372,19 @@ static int run_gemm(const GemmLaunch& L, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-// Decode regime (few rows per expert on average): the GEMM streams weights and is
-// HBM-bound; the weight-major kernel (grouped_gemm_wm.cu) keeps the most weight
-// bytes in flight.  The token-major kernel with 32-row activation tiles remains
+// Decode regime: the GEMM streams weights and is HBM-bound, and the weight-major
+// kernel (grouped_gemm_wm.cu) keeps the most weight bytes in flight — when slots have
+// few rows on average, or when the token-major tiles (128 rows x 128 SwiGLU / 256 down
+// output columns) are too few to give every SM one: a shared expert over a decode batch
+// (one slot, 128 rows, wide weight panels) would otherwise stream its weights with a
+// third of the SMs.  The token-major kernel with 32-row activation tiles remains
 // available (GemmVariant::kTokenMajorSmallM) for comparison.
 static bool decode_regime(const GemmLaunch& L) {
   const int64_t rows = L.rows_hint > 0 ? L.rows_hint : L.rows_cap;
-  return rows <= 48 * static_cast<int64_t>(L.p.P);
+  if (rows <= 48 * static_cast<int64_t>(L.p.P)) return true;
+  const int out_cols = (L.p.w_rows == 2 * L.p.N) ? GM_BM : 2 * GM_BM;  // SwiGLU : down
+  const int64_t token_tiles = ((rows + GM_BM - 1) / GM_BM + L.p.P - 1) * ((L.p.N + out_cols - 1) / out_cols);
+  return token_tiles < num_sms();
 }
 
 // Prefill regime with full 256-row pair tiles on average: the CTA-pair kernel
