@@ -43,7 +43,11 @@ struct PairShape {
   static constexpr int OUT_COLS = SWIGLU ? 128 : 256;  // output columns per tile
   static constexpr int TMEM_COLS = 2 * N;              // two fp32 accumulators
   static constexpr int CTRL_BYTES = 512 + 3 * (G2_MAXP + 1) * 4 + 64;  // + segment lengths, dst rows
-  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + CTRL_BYTES;
+  // down GEMM, rows sent to peers: per epilogue warp, 32 output rows x 64 columns
+  // staged in shared memory (144-byte rows: 128 bytes + 16 of padding)
+  static constexpr int STG_LD = 144;
+  static constexpr int STG_BYTES = SWIGLU ? 0 : 4 * 32 * STG_LD;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + STG_BYTES + CTRL_BYTES;
 };
 
 // tile -> (group, n-tile, m-tile) with 256-row m-tiles, m fastest.  A group is an
@@ -91,7 +95,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * S::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + STAGES * S::B_BYTES);
+  uint8_t* stg = sb + STAGES * S::B_BYTES;  // epilogue staging (down GEMM, peer rows)
+  uint64_t* full = reinterpret_cast<uint64_t*>(stg + S::STG_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -327,6 +332,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS, 1)
               for (int j = 0; j < 32 && col + j < p.N; ++j) orow_ptr[col + j] = hb[j];
             }
           }
+        }
+      } else if (p.peer_out) {
+        // Rows go to other GPUs: a thread holds one output row, so storing straight from
+        // registers would scatter 16-byte pieces over 32 rows per warp instruction, each
+        // a separate small NVLink write.  Stage the warp's 32 rows x 64 columns in shared
+        // memory and store whole 128-byte row segments instead (8 lanes per row, 4 rows
+        // per instruction).
+        uint8_t* my = stg + quarter * (32 * S::STG_LD);
+        const unsigned long long rp = reinterpret_cast<unsigned long long>(orow_ptr);
+        const int vflag = valid ? 1 : 0;
+#pragma unroll 1
+        for (int c = 0; c < S::N; c += 64) {
+          uint32_t v0[32], v1[32];
+          tmem_ld_32x32b_x32(tbase + c, v0);
+          tmem_ld_32x32b_x32(tbase + c + 32, v1);
+          tmem_ld_wait();
+          uint4* srow = reinterpret_cast<uint4*>(my + lane * S::STG_LD);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            srow[q] = make_uint4(pack_bf16x2(__uint_as_float(v0[8 * q]), __uint_as_float(v0[8 * q + 1])),
+                                 pack_bf16x2(__uint_as_float(v0[8 * q + 2]), __uint_as_float(v0[8 * q + 3])),
+                                 pack_bf16x2(__uint_as_float(v0[8 * q + 4]), __uint_as_float(v0[8 * q + 5])),
+                                 pack_bf16x2(__uint_as_float(v0[8 * q + 6]), __uint_as_float(v0[8 * q + 7])));
+            srow[4 + q] = make_uint4(pack_bf16x2(__uint_as_float(v1[8 * q]), __uint_as_float(v1[8 * q + 1])),
+                                     pack_bf16x2(__uint_as_float(v1[8 * q + 2]), __uint_as_float(v1[8 * q + 3])),
+                                     pack_bf16x2(__uint_as_float(v1[8 * q + 4]), __uint_as_float(v1[8 * q + 5])),
+                                     pack_bf16x2(__uint_as_float(v1[8 * q + 6]), __uint_as_float(v1[8 * q + 7])));
+          }
+          __syncwarp();
+          const int col = n * S::OUT_COLS + c;  // a multiple of 64; the pair down GEMM has N % 256 == 0
+#pragma unroll
+          for (int pass = 0; pass < 8; ++pass) {
+            const int row = pass * 4 + (lane >> 3), piece = lane & 7;
+            const unsigned long long dst = __shfl_sync(0xffffffffu, rp, row);
+            const int vrow = __shfl_sync(0xffffffffu, vflag, row);
+            if (vrow) {
+              const uint4 val = reinterpret_cast<const uint4*>(my + row * S::STG_LD)[piece];
+              reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + col)[piece] = val;
+            }
+          }
+          __syncwarp();
         }
       } else {
 #pragma unroll 1
