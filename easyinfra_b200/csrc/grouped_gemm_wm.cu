@@ -37,8 +37,12 @@ struct WmShape {
   static constexpr int TMEM_COLS = (2 * TT < 32) ? 32 : 2 * TT;
   static constexpr int UP_LD = NTOK + 1;                // padded row of the up exchange buffer
   static constexpr int XCHG_BYTES = SWIGLU ? 64 * UP_LD * 4 : 0;
+  // down GEMM, rows sent to peers: one epilogue pass (NTOK tokens x 128 features,
+  // bf16) staged in shared memory, rows padded to 272 bytes
+  static constexpr int STG_LD = WM_M + 8;  // elements
+  static constexpr int STG_BYTES = SWIGLU ? 0 : NTOK * STG_LD * 2;
   static constexpr int CTRL_BYTES = 512 + 2 * (WM_MAXP + 1) * 4;
-  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + XCHG_BYTES + CTRL_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + XCHG_BYTES + STG_BYTES + CTRL_BYTES;
   static_assert(NTOK % 16 == 0 && NTOK >= 16 && TT <= 256, "UMMA N for M = 128");
   static_assert(NTOK <= 32, "epilogue loads NTOK columns per 32x32b.x32 load");
   static_assert(B_BYTES % 1024 == 0, "token buffers keep the 1024-byte swizzle alignment");
@@ -82,7 +86,8 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
   uint8_t* sa = smem;                                   // weights
   uint8_t* sb = smem + STAGES * S::A_BYTES;             // tokens
   float* up_buf = reinterpret_cast<float*>(sb + STAGES * S::B_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sb + STAGES * S::B_BYTES + S::XCHG_BYTES);
+  __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(sb + STAGES * S::B_BYTES + S::XCHG_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + STAGES * S::B_BYTES + S::XCHG_BYTES + S::STG_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -266,19 +271,35 @@ __global__ void __launch_bounds__(WM_THREADS, 1)
             }
           }
           if (h + 1 < passes) epi_bar();  // up_buf is rewritten by the next pass
+        } else if (p.peer_out) {
+          // Rows go to other GPUs.  A thread holds one feature of every token, so each
+          // warp store would carry only 64 bytes of a row over NVLink; stage the pass as
+          // [token][128 features] and store whole 256-byte token rows (16 lanes per row).
+          const int col = n * S::FEAT + feat;
+          if (col < p.N)
+            for (int j = 0; j < nt_h; ++j) stg[j * S::STG_LD + feat] = __float2bfloat16_rn(__uint_as_float(v[j]));
+          epi_bar();
+          const int nfeat = min(S::FEAT, p.N - n * S::FEAT);
+          const int l16 = lane & 15;
+          for (int j = quarter * 2 + (lane >> 4); j < nt_h; j += 8) {
+            const int64_t grow = static_cast<int64_t>(off[e]) + t0 + j;
+            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(peer_out_row(p.po, p.out_row_map[grow], p.ldo * 2)) +
+                                 n * S::FEAT;
+            const __nv_bfloat16* src = stg + j * S::STG_LD;
+            if (l16 * 8 + 8 <= nfeat) {
+              *reinterpret_cast<uint4*>(dst + l16 * 8) = *reinterpret_cast<const uint4*>(src + l16 * 8);
+            } else {
+              for (int f = l16 * 8; f < nfeat; ++f) dst[f] = src[f];
+            }
+          }
+          epi_bar();  // the staging buffer is rewritten by the next pass or tile
         } else {
           const int col = n * S::FEAT + feat;
           if (col < p.N) {
             for (int j = 0; j < nt_h; ++j) {
               int64_t grow = static_cast<int64_t>(off[e]) + t0 + j;
-              __nv_bfloat16* dst;
-              if (p.peer_out) {
-                dst = static_cast<__nv_bfloat16*>(peer_out_row(p.po, p.out_row_map[grow], p.ldo * 2));
-              } else {
-                if (p.out_row_map != nullptr) grow = p.out_row_map[grow];
-                dst = out + grow * p.ldo;
-              }
-              dst[col] = __float2bfloat16_rn(__uint_as_float(v[j]));
+              if (p.out_row_map != nullptr) grow = p.out_row_map[grow];
+              out[grow * p.ldo + col] = __float2bfloat16_rn(__uint_as_float(v[j]));
             }
           }
         }
