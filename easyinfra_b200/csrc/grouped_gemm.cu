@@ -374,16 +374,18 @@ static int run_gemm(const GemmLaunch& L, cudaStream_t stream) {
 
 // Decode regime: the GEMM streams weights and is HBM-bound, and the weight-major
 // kernel (grouped_gemm_wm.cu) keeps the most weight bytes in flight — when slots have
-// few rows on average, or when the token-major tiles (128 rows x 128 SwiGLU / 256 down
-// output columns) are too few to give every SM one: a shared expert over a decode batch
-// (one slot, 128 rows, wide weight panels) would otherwise stream its weights with a
-// third of the SMs.  The token-major kernel with 32-row activation tiles remains
-// available (GemmVariant::kTokenMajorSmallM) for comparison.
+// few rows on average, and, for the down GEMM, also when its token-major tiles (128
+// rows x 256 output columns) are too few to give every SM one: a shared expert over a
+// decode batch, or one expert per rank, would otherwise stream its long-K weights with
+// a tenth of the SMs (measured with 128 rows: Mixtral's down GEMM 92 -> 71 us, Qwen1.5's
+// shared down 39 -> 32 us; the SwiGLU GEMM at those shapes is faster token-major).
+// The token-major kernel with 32-row activation tiles remains available
+// (GemmVariant::kTokenMajorSmallM) for comparison.
 static bool decode_regime(const GemmLaunch& L) {
   const int64_t rows = L.rows_hint > 0 ? L.rows_hint : L.rows_cap;
   if (rows <= 48 * static_cast<int64_t>(L.p.P)) return true;
-  const int out_cols = (L.p.w_rows == 2 * L.p.N) ? GM_BM : 2 * GM_BM;  // SwiGLU : down
-  const int64_t token_tiles = ((rows + GM_BM - 1) / GM_BM + L.p.P - 1) * ((L.p.N + out_cols - 1) / out_cols);
+  if (L.p.w_rows == 2 * L.p.N) return false;  // SwiGLU
+  const int64_t token_tiles = ((rows + GM_BM - 1) / GM_BM + L.p.P - 1) * ((L.p.N + 2 * GM_BM - 1) / (2 * GM_BM));
   return token_tiles < num_sms();
 }
 

@@ -358,17 +358,14 @@ static int run_wm(const GemmLaunch& L, cudaStream_t stream) {
 }
 
 // Wide token tiles (up to 64 rows) pay off when slots carry more than 32 rows: many
-// slots and at least 12 rows per slot on average (skewed routing then puts 32+ rows
+// slots and at least 8 rows per slot on average (skewed routing then puts 32+ rows
 // on the hot slots).  With fewer rows the 10-stage narrow kernel keeps more weight
 // bytes in flight.  wide: 0 = narrow, 1 = wide, -1 = choose.
 int launch_grouped_wm(const GemmLaunch& L, bool swiglu, int wide, cudaStream_t stream) {
   if (L.p.P > WM_MAXP) return -4;
   if (wide < 0) {
     const int64_t rows = L.rows_hint > 0 ? L.rows_hint : L.rows_cap;
-    wide = ((L.p.P >= 32 && rows >= 8 * static_cast<int64_t>(L.p.P)) ||
-            (L.p.P <= 2 && rows > 32 * static_cast<int64_t>(L.p.P)))
-               ? 1
-               : 0;
+    wide = (L.p.P >= 32 && rows >= 8 * static_cast<int64_t>(L.p.P)) ? 1 : 0;
   }
   if (wide) return swiglu ? run_wm<32, 8, true, true>(L, stream) : run_wm<32, 8, false, true>(L, stream);
   return swiglu ? run_wm<32, 10, true, false>(L, stream) : run_wm<32, 10, false, false>(L, stream);
