@@ -227,13 +227,18 @@ __global__ void __launch_bounds__(256) router_logits_gemv_cols(RouterLogitsParam
   const int nt = min(RG, p.T - t0);
   constexpr int V = 16 / sizeof(E);
   const E* x = static_cast<const E*>(p.x) + static_cast<int64_t>(t0) * p.ldx;
-  uint4 xv[NX][RG];
+  // the token rows in fp32, converted once for all of the CTA's columns (exact)
+  float xf[NX][RG][V];
 #pragma unroll
   for (int j = 0; j < NX; ++j) {
     const int c = (threadIdx.x + j * 256) * V;
 #pragma unroll
-    for (int i = 0; i < RG; ++i)
-      xv[j][i] = (i < nt) ? __ldg(reinterpret_cast<const uint4*>(x + i * p.ldx + c)) : make_uint4(0, 0, 0, 0);
+    for (int i = 0; i < RG; ++i) {
+      const uint4 u = (i < nt) ? __ldg(reinterpret_cast<const uint4*>(x + i * p.ldx + c)) : make_uint4(0, 0, 0, 0);
+      const E* ue = reinterpret_cast<const E*>(&u);
+#pragma unroll
+      for (int q = 0; q < V; ++q) xf[j][i][q] = static_cast<float>(ue[q]);
+    }
   }
   const E* wbase = static_cast<const E*>(p.w) + static_cast<int64_t>(col0) * p.H;
   uint4 wv[NX];
@@ -254,11 +259,13 @@ __global__ void __launch_bounds__(256) router_logits_gemv_cols(RouterLogitsParam
 #pragma unroll
     for (int j = 0; j < NX; ++j) {
       const E* we = reinterpret_cast<const E*>(&wv[j]);
+      float wf[V];
+#pragma unroll
+      for (int q = 0; q < V; ++q) wf[q] = static_cast<float>(we[q]);
 #pragma unroll
       for (int i = 0; i < RG; ++i) {
-        const E* xe = reinterpret_cast<const E*>(&xv[j][i]);
 #pragma unroll
-        for (int q = 0; q < V; ++q) acc[i] = fmaf(static_cast<float>(xe[q]), static_cast<float>(we[q]), acc[i]);
+        for (int q = 0; q < V; ++q) acc[i] = fmaf(xf[j][i][q], wf[q], acc[i]);
       }
     }
 #pragma unroll
