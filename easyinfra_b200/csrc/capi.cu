@@ -333,9 +333,15 @@ int add_rmsnorm_router_impl(const void* residual, const void* hidden, const void
   const bool with_permute = send != nullptr || pos_of != nullptr;
   if (with_permute && (!send || !pos_of || !aligned16(send) || (static_cast<int64_t>(H) * eb) % 16 != 0))
     return fail(B200MOE_EINVAL, "send and pos_of must both be given, send 16-byte aligned with 16-byte rows");
-  const bool fuse = router_small_fused_ok(T, H, x_dtype, num_slots, 0, true);
+  // The fused kernel writes residual_out from its first CTA while the others still read
+  // residual: an in-place add runs the separate kernels (one CTA per row) instead.
+  const int64_t span = T > 0 ? ((T - 1) * ld + H) * eb : 0;
+  const char* r0 = static_cast<const char*>(residual);
+  const char* o0 = static_cast<const char*>(residual_out);
+  const bool in_place = hidden != nullptr && T > 0 && o0 < r0 + span && r0 < o0 + span;
+  const bool fuse = !in_place && router_small_fused_ok(T, H, x_dtype, num_slots, 0, true);
   if (!fuse) {
-    // larger batches: the prologue kernel, then the router on its output (then the permute)
+    // the prologue kernel, then the router on its output (then the permute)
     if ((rc = b200moe_add_rmsnorm(residual, hidden, norm_weight, eps, T, H, x_dtype, ld, residual_out, normed,
                                   ld_normed, stream)))
       return rc;

@@ -148,6 +148,21 @@ def _router_launches(T: int) -> int:
     return 0 if T == 0 else (1 if T <= 8 else 2)
 
 
+def _in_place(residual: torch.Tensor, hidden: Optional[torch.Tensor], ro: torch.Tensor) -> bool:
+    # the C-ABI runs the separate kernels when residual_out overlaps residual under an add
+    if hidden is None or residual.shape[0] == 0:
+        return False
+    span = ((residual.shape[0] - 1) * residual.stride(0) + residual.shape[1]) * residual.element_size()
+    r0, o0 = residual.data_ptr(), ro.data_ptr()
+    return o0 < r0 + span and r0 < o0 + span
+
+
+def _prologue_router_launches(T: int, in_place: bool) -> int:
+    if T == 0:
+        return 0
+    return 1 if T <= 8 and not in_place else 1 + _router_launches(T)
+
+
 def router(x: torch.Tensor, gate_w: torch.Tensor, top_k: int, *, renorm: bool,
            gate_bias: Optional[torch.Tensor] = None, scale: float = 1.0,
            has_shared_gate: bool = False, log2phy: Optional[torch.Tensor] = None,
@@ -180,7 +195,8 @@ def add_rmsnorm_router(residual: torch.Tensor, hidden: Optional[torch.Tensor], n
     RouterOutput); bit-identical to add_rmsnorm followed by router.  With permute=True
     the routed rows are permuted too (in the same launch up to 8 tokens; `send` is the
     optional [>= T*K, H] send buffer) and a PermuteOutput is returned fourth,
-    bit-identical to calling permute afterwards."""
+    bit-identical to calling permute afterwards.  An in-place add (residual_out
+    overlapping residual) runs the separate kernels."""
     _need_cuda(residual, hidden, norm_weight, gate_w, gate_bias, log2phy, rep_count, status)
     residual = _rows_contig(residual)
     T, H = residual.shape
@@ -199,7 +215,7 @@ def add_rmsnorm_router(residual: torch.Tensor, hidden: Optional[torch.Tensor], n
     if not permute:
         _lib.call("b200moe_add_rmsnorm_router", *head, *_router_tail(o, T, H, top_k, renorm, scale,
                                                                      has_shared_gate, status))
-        _count(0 if T == 0 else (1 if T <= 8 else 3))
+        _count(_prologue_router_launches(T, _in_place(residual, hidden, ro)))
         return ro, nm, _router_result(o)
     if nm.stride(0) != H:
         raise ValueError("the permute reads normed rows with row stride H")
@@ -212,7 +228,8 @@ def add_rmsnorm_router(residual: torch.Tensor, hidden: Optional[torch.Tensor], n
     # send and pos_of go after logits_out
     tail[-4:-4] = [sb.data_ptr(), pos_of.data_ptr()]
     _lib.call("b200moe_add_rmsnorm_router_permute", *head, *tail)
-    _count(0 if T == 0 else (1 if T <= 8 else 4))
+    in_place = _in_place(residual, hidden, ro)
+    _count(_prologue_router_launches(T, in_place) + (1 if T > 8 or in_place else 0))
     return ro, nm, _router_result(o), PermuteOutput(sb, pos_of, None, None)
 
 

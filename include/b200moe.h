@@ -110,7 +110,8 @@ B200MOE_API int b200moe_router(const void* x, int64_t ldx, int x_dtype, const vo
  * dimension ld for residual / hidden / residual_out and ld_normed for normed), then
  * b200moe_router on normed (same remaining arguments).  For T <= 8 (decode) the whole
  * of it is one launch: every router-column CTA builds the normed rows itself and the
- * last CTA selects; larger batches run the two calls.  Results are bit-identical to
+ * last CTA selects.  Larger batches, and an in-place add (residual_out overlapping
+ * residual with hidden given), run the two calls.  Results are bit-identical to
  * calling b200moe_add_rmsnorm and b200moe_router.  Replaces the routing step of
  * MoeAll2AllBlock.all2all_chunk_routing_compute (easyinfra/generation/blocks/moe/
  * moe_all2all.py:331-343) together with Qwen3MoeSparseMoeBlock._routing

@@ -421,23 +421,48 @@ def test_small_batch_fused_router_equals_two_kernel_path(cuda_device, T, E, H, s
         assert torch.equal(small.shared_gate, sel.shared_gate)
 
 
-@pytest.mark.parametrize("T", [1, 5, 8, 12])
-def test_fused_prologue_router_equals_separate_calls(cuda_device, T):
-    """add_rmsnorm_router (one launch up to 8 tokens) == add_rmsnorm then router."""
-    g = torch.Generator().manual_seed(T)
-    H, E = 2048, 128
-    res = torch.randn(T, H, generator=g).to(torch.bfloat16).to(cuda_device)
-    hid = torch.randn(T, H, generator=g).to(torch.bfloat16).to(cuda_device)
-    nw = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(cuda_device)
-    w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
-    ro, nm, r = ops.add_rmsnorm_router(res, hid, nw, 1e-6, w, 8, renorm=True)
+@pytest.mark.parametrize("T", [1, 5, 8, 12, 64])
+@pytest.mark.parametrize("E,H,K,with_hidden", [(128, 2048, 8, True), (8, 4096, 2, True), (128, 2048, 8, False),
+                                               (60, 1024, 4, True)])
+def test_fused_prologue_router_equals_separate_calls(cuda_device, T, E, H, K, with_hidden):
+    """add_rmsnorm_router equals add_rmsnorm then router bit for bit: one launch up to 8
+    tokens (every router-column CTA builds the normed rows), the separate kernels above."""
+    g = torch.Generator().manual_seed(T * 31 + E + H)
+    d = cuda_device
+    res = torch.randn(T, H, generator=g).to(torch.bfloat16).to(d)
+    hid = torch.randn(T, H, generator=g).to(torch.bfloat16).to(d) if with_hidden else None
+    nw = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(d)
+    w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).to(d)
+    ro, nm, r = ops.add_rmsnorm_router(res, hid, nw, 1e-6, w, K, renorm=True)
     ro2, nm2 = ops.add_rmsnorm(res, hid, nw, 1e-6)
-    r2 = ops.router(nm2, w, 8, renorm=True)
+    r2 = ops.router(nm2, w, K, renorm=True)
     torch.cuda.synchronize()
     assert torch.equal(ro, ro2) and torch.equal(nm, nm2)
     for a, c in [(r.topk_ids, r2.topk_ids), (r.topk_weights, r2.topk_weights), (r.phys_ids, r2.phys_ids),
                  (r.slot_counts, r2.slot_counts), (r.slot_offsets, r2.slot_offsets)]:
         assert torch.equal(a, c)
+
+
+@pytest.mark.parametrize("T", [5, 64])
+def test_fused_prologue_router_in_place_add(cuda_device, T):
+    """residual_out aliasing residual (an in-place add): the one-launch form would read
+    rows its first CTA already overwrote, so the call takes the separate kernels (one
+    CTA per row, safe in place) and equals them run on a copy."""
+    g = torch.Generator().manual_seed(500 + T)
+    H, E, K = 2048, 128, 8
+    d = cuda_device
+    res = torch.randn(T, H, generator=g).to(torch.bfloat16).to(d)
+    hid = torch.randn(T, H, generator=g).to(torch.bfloat16).to(d)
+    nw = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(d)
+    w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).to(d)
+    ro2, nm2 = ops.add_rmsnorm(res.clone(), hid, nw, 1e-6)
+    r2 = ops.router(nm2, w, K, renorm=True)
+    ro, nm, r = ops.add_rmsnorm_router(res, hid, nw, 1e-6, w, K, renorm=True, residual_out=res)
+    torch.cuda.synchronize()
+    assert ro.data_ptr() == res.data_ptr()
+    assert torch.equal(res, ro2) and torch.equal(nm, nm2)
+    assert torch.equal(r.topk_ids, r2.topk_ids) and torch.equal(r.topk_weights, r2.topk_weights)
+    assert torch.equal(r.slot_offsets, r2.slot_offsets)
 
 
 @pytest.mark.parametrize("T", [1, 3, 8, 12])
