@@ -77,3 +77,48 @@ def test_exchange_descriptor_and_layout_without_a_gpu():
     bad = ctypes.c_int64()
     assert lib.b200moe_ep_layout(9, 4, 1, 1, 1024, None, None, ctypes.byref(bad)) != 0   # > 8 ranks
     assert lib.b200moe_ep_layout(2, 4, 1, 1, 1000, None, None, ctypes.byref(bad)) != 0   # rows not 16-B multiples
+
+
+def _declared_signatures():
+    """{name: [parameter type strings]} for every B200MOE_API declaration."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"B200MOE_API\s+([\w\s\*]+?)\b(b200moe_\w+)\s*\(([^)]*)\)\s*;", text):
+        params = [p.strip() for p in m.group(3).split(",") if p.strip()]
+        if params == ["void"]:
+            params = []
+        out[m.group(2)] = (m.group(1).strip(), params)
+    return out
+
+
+def _ctype_of(decl: str):
+    """The ctypes type a C parameter declaration should map to."""
+    d = " ".join(decl.replace("*", " * ").split())
+    if "*" in d:
+        return "ptr"
+    base = d.rsplit(" ", 1)[0] if " " in d else d
+    base = base.replace("const ", "").strip()
+    return {"int": "int", "int64_t": "int64", "size_t": "size", "float": "float", "uint64_t": "uint64",
+            "uint32_t": "uint32"}.get(base, base)
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every entry point's ctypes argument list has the header's arity and kinds
+    (pointer / int / int64 / size_t / float) and the same return kind, so a changed
+    C signature cannot be called with a stale Python table."""
+    kinds = {ctypes.c_void_p: "ptr", ctypes.c_char_p: "ptr", ctypes.c_int: "int", ctypes.c_int64: "int64",
+             ctypes.c_size_t: "size", ctypes.c_float: "float", ctypes.c_uint64: "uint64",
+             ctypes.c_uint32: "uint32"}
+    decl = _declared_signatures()
+    assert set(decl) == set(_lib.SIGNATURES)
+    for name, (ret, params) in decl.items():
+        restype, argtypes = _lib.SIGNATURES[name]
+        want = [_ctype_of(p) for p in params]
+        got = [kinds.get(a, "ptr" if a is not None and issubclass(a, ctypes._Pointer) else str(a))
+               for a in argtypes]
+        # size_t and uint64 are the same width on this platform's ABI; int64 likewise
+        norm = {"size": "u64", "uint64": "u64", "int64": "i64"}
+        assert [norm.get(k, k) for k in got] == [norm.get(k, k) for k in want], (name, got, want)
+        ret_kind = _ctype_of(ret + " x")
+        got_ret = "ptr" if restype in (ctypes.c_char_p, ctypes.c_void_p) else kinds.get(restype, str(restype))
+        assert norm.get(got_ret, got_ret) == norm.get(ret_kind, ret_kind), (name, got_ret, ret_kind)
